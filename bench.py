@@ -1,0 +1,343 @@
+"""Benchmark of the SSD prefill scan (one JSON line on rank 0).
+
+Workload: per rank, S=1, L=8192, H=64, P=64, N=128, G=8,
+x/B/C bf16, dt/A/s0 f32, y/s1 f32, multipass.  Under torchrun each rank owns
+its own block of 64 heads of a head-sharded layer (no collective on the data
+path: "scaling": "weak"); `value` counts C3-equivalent tokens, i.e. tokens x
+(heads processed / 64), summed over ranks, over the max device time of any
+rank.
+
+Timing: W warm-up steps, then K steps; before each step a 256 MiB buffer is
+written (flushing the 126 MB L2; the flush is outside the timed events); each
+step is bracketed by CUDA events on the launching stream; barrier +
+synchronize on both sides of the loop; max over ranks.
+
+Also reported: per-kernel attribution and roofline (the output kernel is the
+dominant one), e2e through the C ABI with pinned host buffers (H2D of the
+step's inputs and D2H of y and s1 inside the timed region), the CPU baseline
+(the reference's own fp64 oracle, compiled from its sources into oracle/_ref,
+run over (seq, head) slices on all host cores, on a bounded sample), and SM
+clocks sampled during the timed region.
+
+--impl reference times the reference's CPU implementation alone (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "SSD prefill tok/s and % of TC/HBM roofline, L=8192 H64 P64 N128, 1/2/4/8 B200"
+UNIT = "tok/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--compute", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--cpu-sample-tokens", type=int, default=2048)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own oracle (or our restatement) on host cores.
+# ---------------------------------------------------------------------------
+def cpu_baseline(shape, sample_tokens: int):
+    import numpy as np
+
+    from helix_b200.synth import make_inputs, to_numpy_f32
+    from oracle.oracle import Oracle, Reference, available_reference
+
+    kind = "reference" if available_reference() else "port"
+    impl = Reference() if kind == "reference" else Oracle()
+    T = min(sample_tokens, shape.L)
+    sub = type(shape)(shape.S, T, shape.H, shape.P, shape.N, shape.G, shape.io)
+    t = make_inputs(sub, seed=99)
+    prob = {k: np.ascontiguousarray(to_numpy_f32(t[k])) for k in ("s0", "x", "dt", "A", "B", "C")}
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    base = Oracle().desc_init(T, sub.S, sub.H, sub.P, sub.N, sub.G)
+    y = np.zeros((sub.S, T, sub.H, sub.P), np.float32)
+    s1 = np.zeros((sub.S, sub.H, sub.P, sub.N), np.float32)
+    F = C.POINTER(C.c_float)
+    fn = getattr(impl.lib, "ref_scan" if kind == "reference" else "oracle_scan")
+    hpg = sub.H // sub.G
+
+    # One call per (seq, head) slice: a descriptor with n_head = n_group = 1
+    # and pointers offset to the slice, exactly the reference's own code per
+    # slice; ctypes releases the GIL, so the slices run on all cores.
+    def slice_call(seq, h):
+        from helix_b200.abi import ScanDesc
+        d = ScanDesc()
+        C.memmove(C.byref(d), C.byref(base), C.sizeof(ScanDesc))
+        d.n_head, d.n_group, d.n_seq = 1, 1, 1
+        g = h // hpg
+        off = lambda a, i: C.cast(a.ctypes.data + 4 * i, F)  # noqa: E731
+        fn(C.byref(d), off(prob["s0"], seq * base.seq_s + h * base.s_s[0]),
+           off(prob["x"], seq * base.seq_x + h * base.s_x[1]),
+           off(prob["dt"], seq * base.seq_dt + h * base.s_dt[1]), off(prob["A"], h),
+           off(prob["B"], seq * base.seq_b + g * base.s_b[1]),
+           off(prob["C"], seq * base.seq_c + g * base.s_c[1]), None,
+           off(y, seq * base.seq_y + h * base.s_y[1]), off(s1, seq * base.seq_s + h * base.s_s[0]))
+
+    from concurrent.futures import ThreadPoolExecutor
+    jobs = [(s, h) for s in range(sub.S) for h in range(sub.H)]
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=cores) as ex:
+        list(ex.map(lambda a: slice_call(*a), jobs))
+    sec = time.perf_counter() - t0
+    value = sub.S * T / sec  # tokens of the full H-head layer per second
+    return dict(value=value, unit=UNIT, cores=cores, kind=kind,
+                sample=f"{T} of {shape.L} tokens, all {sub.H} heads, S={sub.S}; "
+                       f"{'helix::ref::scan (reference sources)' if kind == 'reference' else 'oracle_scan (C port)'}"
+                       f" per (seq, head) slice on {cores} threads; {sec:.2f} s wall")
+
+
+# ---------------------------------------------------------------------------
+class Clocks:
+    """nvidia-smi sampler for the timed region."""
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.rows = index, None, []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    from helix_b200.synth import Shape
+    shape = Shape.of(a.config)
+
+    if a.impl == "reference":
+        if rank != 0:
+            return 0
+        steps = []
+        cb = None
+        for i in range(a.warmup + a.steps):
+            cb = cpu_baseline(shape, a.cpu_sample_tokens)
+            if i >= a.warmup:
+                steps.append(cb["value"])
+        v = statistics.median(steps)
+        cb["value"] = v
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * shape.S * shape.L / v,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded, BASELINE distributions)",
+            "config": {"workload": f"{a.config}: S={shape.S} L={shape.L} H={shape.H} P={shape.P} "
+                                   f"N={shape.N} G={shape.G}; CPU sample per step",
+                       "sample": cb["sample"]},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    import helix_b200
+    from helix_b200 import abi
+    from helix_b200.synth import make_inputs
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    ctx = helix_b200.Context(local)
+    t = make_inputs(shape, seed=1000 + rank, device=dev)
+    if a.compute == "f32" and shape.io == "bf16":
+        pass  # exact fp32 kernels reading bf16 operands
+    x, dt, A, B, Cm, s0 = t["x"], t["dt"], t["A"], t["B"], t["C"], t["s0"]
+    y = torch.empty(x.shape, dtype=torch.float32, device=dev)
+    s1 = torch.empty_like(s0)
+    d = helix_b200.desc_from_tensors(x, dt, B, s0, y, multipass=True, compute=a.compute)
+    if not ctx.supported(d):
+        raise SystemExit(f"descriptor unsupported: {ctx.last_error()}")
+    nbytes = ctx.scratch_size(d)
+    scratch = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        st = ctx.encode(d, s0, x, dt, A, B, Cm, y, s1, scratch=scratch, stream=stream)
+        if st != abi.HELIX_OK:
+            raise SystemExit(f"encode failed: {ctx.last_error()}")
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def timed(fn, k, pre=None):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k)]
+        barrier()
+        for e0, e1 in evs:
+            flush.fill_(1)
+            if pre:
+                pre()
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+        barrier()
+        return [e0.elapsed_time(e1) for e0, e1 in evs]
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        tt = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        return float(tt.item())
+
+    for _ in range(a.warmup):
+        flush.fill_(1)
+        step()
+    barrier()
+    with Clocks(local) as clk:
+        ms = timed(step, a.steps)
+    total_ms = max_over_ranks(sum(ms))
+    ms_per_step = total_ms / a.steps
+    launches = 2 if nbytes > 0 else 1
+
+    # ---- per-kernel attribution (same steps, passes split) --------------
+    def only(p):
+        def f():
+            os.environ["HELIX_ONLY_PASS"] = p
+            try:
+                step()
+            finally:
+                os.environ.pop("HELIX_ONLY_PASS", None)
+        return f
+    ms_c = max_over_ranks(sum(timed(only("C"), a.steps))) / a.steps
+    ms_a = max_over_ranks(sum(timed(only("A"), a.steps))) / a.steps if launches == 2 else 0.0
+
+    hbm, tc, peak_kind = peaks()
+    e_io = 2 if shape.io == "bf16" else 4
+    n_x = shape.S * shape.L * shape.H * shape.P
+    n_bc = shape.S * shape.L * shape.G * shape.N
+    n_st = shape.S * shape.H * shape.P * shape.N
+    # Output kernel's algorithmic bytes per launch: x, B, C, dt read once,
+    # y written once, s0 read and s1 written once.
+    out_bytes = n_x * e_io + 2 * n_bc * e_io + shape.S * shape.L * shape.H * 4 + n_x * 4 + 2 * n_st * 4
+    achieved = out_bytes / (ms_c * 1e-3) / 1e9
+    path_gbs = shape.alg_bytes() / (ms_per_step * 1e-3) / 1e9
+    tflops = shape.flops() / (ms_per_step * 1e-3) / 1e12
+
+    # ---- e2e through the C ABI with host buffers ------------------------
+    e2e = None
+    if not a.no_e2e:
+        host = {k: v.to("cpu").pin_memory() for k, v in dict(x=x, dt=dt, A=A, B=B, C=Cm, s0=s0).items()}
+        yh = torch.empty(y.shape, dtype=torch.float32, pin_memory=True)
+        sh = torch.empty(s1.shape, dtype=torch.float32, pin_memory=True)
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = yh.numel() * 4 + sh.numel() * 4
+
+        def e2e_step():
+            for k, v in host.items():
+                dict(x=x, dt=dt, A=A, B=B, C=Cm, s0=s0)[k].copy_(v, non_blocking=True)
+            step()
+            yh.copy_(y, non_blocking=True)
+            sh.copy_(s1, non_blocking=True)
+        for _ in range(2):
+            e2e_step()
+        ems = max_over_ranks(sum(timed(e2e_step, max(3, a.steps // 4)))) / max(3, a.steps // 4)
+        e2e = {"value": world * shape.S * shape.L / (ems * 1e-3), "unit": UNIT, "ms_per_step": ems,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+    value = world * shape.S * shape.L * (shape.H / 64.0) / (ms_per_step * 1e-3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16" if a.compute == "bf16" else "f32",
+        "data": "synthetic (seeded, BASELINE distributions; random A, B, C, x, dt)",
+        "config": {"workload": f"{a.config}: S={shape.S} L={shape.L} H={shape.H} P={shape.P} N={shape.N} "
+                               f"G={shape.G}, x/B/C {shape.io}, dt/A/s0/y/s1 f32, multipass; per rank one "
+                               f"64-head block of a head-sharded layer",
+                   "l2": "flushed before every timed step (256 MiB write, untimed)",
+                   "compute": a.compute, "runs_plan_scratch_bytes": nbytes,
+                   "tflops": tflops, "path_alg_bytes": shape.alg_bytes(), "path_gbs": path_gbs,
+                   "path_hbm_frac": path_gbs / hbm,
+                   "kernels_ms": {"state": ms_a, "output": ms_c}},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": None, "kernel": "output kernel",
+                     "alg_bytes_per_launch": out_bytes, "peak_kind": peak_kind},
+        "gpu_launches": launches * a.steps,
+        "clocks": clk.summary(),
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(shape, a.cpu_sample_tokens)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,134 @@
+"""helix_b200 -- B200-native (sm_100a) Mamba-2 SSD prefill scan behind the
+HELIX C ABI.
+
+The product is ``libhelix.so`` (C ABI in include/helix/helix.h).  This module
+is a thin host-side convenience over it for PyTorch users: it maps torch
+tensors (device memory) and the current CUDA stream onto the ABI's
+``helix_tensor`` / ``cudaStream_t`` arguments.  There is no Python compute
+path: every call goes through the library, and a missing library raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+from . import abi
+
+__all__ = ["HelixError", "Context", "desc_from_tensors", "scan", "abi"]
+
+
+class HelixError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"helix status {abi.STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status
+
+
+def _t(x) -> abi.Tensor:
+    """torch tensor (or None) -> helix_tensor."""
+    if x is None:
+        return abi.NULL_TENSOR
+    return abi.Tensor(C.c_void_p(x.data_ptr()), 0)
+
+
+class Context:
+    """Owns one helix_ctx bound to a CUDA device."""
+
+    def __init__(self, device: Optional[int] = None):
+        self.lib = abi.load()
+        h = C.c_void_p()
+        dev = C.c_int(device) if device is not None else None
+        st = self.lib.helix_ctx_create(C.byref(h), C.byref(dev) if dev is not None else None, None)
+        if st != abi.HELIX_OK:
+            raise HelixError(st, self.lib.helix_ctx_last_error(None).decode())
+        self.handle = h
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.helix_ctx_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def last_error(self) -> str:
+        return self.lib.helix_ctx_last_error(self.handle).decode()
+
+    def supported(self, d: abi.ScanDesc) -> bool:
+        return bool(self.lib.helix_scan_supported(self.handle, C.byref(d)))
+
+    def scratch_size(self, d: abi.ScanDesc) -> int:
+        return int(self.lib.helix_scan_scratch_size(self.handle, C.byref(d)))
+
+    def select_backend(self, d: abi.ScanDesc) -> int:
+        return int(self.lib.helix_ctx_select_backend(self.handle, C.byref(d)))
+
+    def backend_desc(self, d: abi.ScanDesc) -> str:
+        return self.lib.helix_ctx_backend_desc(self.handle, C.byref(d)).decode()
+
+    def encode(self, d: abi.ScanDesc, s0, x, dt, A, B, Cm, y, s1, ids=None, scratch=None,
+               stream=None, into: bool = False) -> int:
+        """Enqueues one scan on `stream` (a torch.cuda.Stream, a raw handle, or
+        None for torch's current stream).  Returns the helix_status."""
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream(x.device)
+        handle = getattr(stream, "cuda_stream", stream)
+        fn = self.lib.helix_scan_encode_into if into else self.lib.helix_scan_encode
+        return int(fn(self.handle, C.c_void_p(handle), C.byref(d), _t(s0), _t(x), _t(dt), _t(A),
+                      _t(B), _t(Cm), _t(ids), _t(y), _t(s1), _t(scratch)))
+
+
+def desc_from_tensors(x, dt, B, s0, y=None, *, multipass: bool = True, compute: str = "auto",
+                      backend: int = abi.HELIX_BACKEND_AUTO) -> abi.ScanDesc:
+    """Descriptor for torch tensors laid out as in helix.h:
+    x (S, L, H, P), dt (S, L, H), B and C (S, L, G, N), s0 (S, H, P, N),
+    y (S, L, H, P).  Strides are taken from the tensors, so views work."""
+    import torch
+    S, L, H, P = x.shape
+    G, N = B.shape[2], B.shape[3]
+    d = abi.desc_init(L, S, H, P, N, G)
+    d.s_x[:] = list(x.stride()[1:]); d.seq_x = x.stride(0)
+    d.s_b[:] = list(B.stride()[1:]); d.seq_b = B.stride(0)
+    d.s_c[:] = list(B.stride()[1:]); d.seq_c = B.stride(0)
+    d.s_dt[:] = list(dt.stride()[1:]); d.seq_dt = dt.stride(0)
+    d.s_s[:] = list(s0.stride()[1:]); d.seq_s = s0.stride(0)
+    if y is not None:
+        d.s_y[:] = list(y.stride()[1:]); d.seq_y = y.stride(0)
+    d.io_dtype = abi.HELIX_BF16 if x.dtype == torch.bfloat16 else abi.HELIX_F32
+    if compute == "auto":
+        compute = "bf16" if x.dtype == torch.bfloat16 else "f32"
+    d.compute_dtype = abi.HELIX_BF16 if compute == "bf16" else abi.HELIX_F32
+    d.backend = backend
+    d.multipass = multipass
+    return d
+
+
+_default_ctx: dict[int, Context] = {}
+
+
+def scan(x, dt, A, B, Cm, s0, ids=None, *, multipass: bool = True, compute: str = "auto",
+         backend: int = abi.HELIX_BACKEND_AUTO, ctx: Optional[Context] = None, stream=None):
+    """Runs the scan on torch CUDA tensors and returns (y, s1).
+
+    Allocates y, s1 and the scratch with torch (this convenience wrapper is
+    the only place that allocates; the library itself never does)."""
+    import torch
+    dev = x.device.index if x.device.index is not None else torch.cuda.current_device()
+    if ctx is None:
+        ctx = _default_ctx.get(dev) or _default_ctx.setdefault(dev, Context(dev))
+    y = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    s1 = torch.empty(s0.shape, dtype=torch.float32, device=x.device)
+    d = desc_from_tensors(x, dt, B, s0, y, multipass=multipass, compute=compute, backend=backend)
+    if Cm.stride() != B.stride():
+        d.s_c[:] = list(Cm.stride()[1:]); d.seq_c = Cm.stride(0)
+    nbytes = ctx.scratch_size(d)
+    scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device) if nbytes else None
+    st = ctx.encode(d, s0, x, dt, A, B, Cm, y, s1, ids=ids, scratch=scratch, stream=stream)
+    if scratch is not None and stream is not None and hasattr(stream, "cuda_stream"):
+        scratch.record_stream(stream)
+    if st != abi.HELIX_OK:
+        raise HelixError(st, ctx.last_error())
+    return y, s1

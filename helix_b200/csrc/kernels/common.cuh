@@ -1,0 +1,63 @@
+// common.cuh -- device helpers shared by both kernel families.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "../runtime/internal.h"
+
+namespace hx {
+
+// softplus with the v > 20 shortcut, then the clamp
+// (reference src/kernels/helix_common.h:14-20, src/reference/scan_ref.cpp:13-24).
+__device__ __forceinline__ float dt_of(float raw, float lo, float hi) {
+    float v = raw > 20.0f ? raw : log1pf(expf(raw));
+    v = v < lo ? lo : v;
+    v = v > hi ? hi : v;
+    return v;
+}
+
+template <bool BF16>
+__device__ __forceinline__ float ld_io(const void* base, int64_t i) {
+    if constexpr (BF16)
+        return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
+    else
+        return static_cast<const float*>(base)[i];
+}
+
+// Inclusive prefix sum over the first `n` threads of the block (n <= 32 *
+// warps).  Every thread of the block must call it.  `tot` holds one float per
+// warp.  Returns the prefix for threads < n (others get an unspecified value).
+__device__ __forceinline__ float block_prefix(float v, int n, float* tot) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+    }
+    if (lane == 31) tot[warp] = v;
+    __syncthreads();
+    const int nw = (n + 31) >> 5;
+    float add = 0.0f;
+    for (int w = 0; w < warp && w < nw; ++w) add += tot[w];
+    __syncthreads();
+    return v + add;
+}
+
+// Flattened CTA index -> (seq, run, head, slab), slab fastest, then head, so
+// the CTAs of one group's heads run next to each other and share B/C in L2.
+struct Tile {
+    int seq, run, h, slab;
+};
+__device__ __forceinline__ Tile decode_tile(int b, int n_pslab, int H, int n_runs) {
+    Tile t;
+    t.slab = b % n_pslab;
+    b /= n_pslab;
+    t.h = b % H;
+    b /= H;
+    t.run = b % n_runs;
+    t.seq = b / n_runs;
+    return t;
+}
+
+}  // namespace hx

@@ -1,0 +1,163 @@
+// caps.cpp -- which descriptors run, on which kernel family, with what plan.
+//
+// Replaces reference src/runtime/caps.mm:18-304.  helix_scan_supported() is
+// still the contract with the host: false means "keep your own kernel", and
+// nothing is ever enqueued for a descriptor it rejects.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <string>
+
+#include "internal.h"
+
+namespace hx {
+
+namespace {
+
+bool positive_dims(const helix_scan_desc& d) {
+    return d.n_tok > 0 && d.n_seq > 0 && d.n_head > 0 && d.head_dim > 0 && d.d_state > 0 &&
+           d.n_group > 0;
+}
+
+// Scratch budget for run states, MiB.  Plays the role of the reference's
+// HELIX_SCRATCH_MB (src/runtime/caps.mm:166-176): a smaller budget means
+// fewer runs (less parallelism), never a wrong answer.
+size_t scratch_budget() {
+    if (const char* e = std::getenv("HELIX_SCRATCH_MB")) {
+        const long mb = std::strtol(e, nullptr, 10);
+        if (mb > 0) return (size_t)mb << 20;
+    }
+    return (size_t)512 << 20;
+}
+
+// Test and tuning hook: force the run length (tokens, rounded up to a
+// multiple of kRunQuantum).  Small values put many runs in flight, which is
+// what exercises the run-to-run state carry.
+int forced_run_tokens() {
+    if (const char* e = std::getenv("HELIX_RUN_TOKENS")) {
+        const long v = std::strtol(e, nullptr, 10);
+        if (v > 0) return (int)((v + kRunQuantum - 1) / kRunQuantum * kRunQuantum);
+    }
+    return 0;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+}  // namespace
+
+// Precision selects the kernel family:
+//   backend REF or SGMMA          -> exact fp32 (the reference's fp32 paths)
+//   backend MPP                   -> tcgen05 bf16 (the reference's bf16 path)
+//   backend AUTO                  -> compute_dtype decides
+Path select_path(const helix_scan_desc& d) {
+    if (d.backend == HELIX_BACKEND_REF || d.backend == HELIX_BACKEND_SGMMA) return kPathSimtF32;
+    if (d.backend == HELIX_BACKEND_MPP) return kPathTcBf16;
+    return d.compute_dtype == HELIX_BF16 ? kPathTcBf16 : kPathSimtF32;
+}
+
+bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why) {
+    auto no = [&](const char* m) {
+        if (why) *why = m;
+        return false;
+    };
+    if (!ctx) return no("null context");
+    if (!positive_dims(d)) return no("non-positive dimension");
+    if (d.n_head % d.n_group != 0) return no("n_head not a multiple of n_group");
+    // Only the scalar decay admits the chunked reassociation
+    // (reference src/runtime/caps.mm:121-123).
+    if (d.a_form != HELIX_A_SCALAR_PER_HEAD) return no("diagonal A is not accelerated");
+    if (d.io_dtype != HELIX_F32 && d.io_dtype != HELIX_BF16) return no("io_dtype must be F32 or BF16");
+    if (d.compute_dtype != HELIX_F32 && d.compute_dtype != HELIX_BF16)
+        return no("compute_dtype must be F32 or BF16");
+    if (d.backend < HELIX_BACKEND_AUTO || d.backend > HELIX_BACKEND_REF) return no("unknown backend");
+    // The kernels read B, C and the states with unit innermost stride
+    // (reference src/runtime/caps.mm:136-139).
+    if (d.s_b[2] != 1 || d.s_c[2] != 1 || d.s_s[2] != 1) return no("innermost B/C/state stride must be 1");
+    if (d.chunk != 0 && d.chunk != 64 && d.chunk != 128) return no("chunk must be 0, 64 or 128");
+    // Run bookkeeping and grid sizes are int32.
+    if ((int64_t)d.n_seq * d.n_head * ((d.head_dim + kSlab - 1) / kSlab) *
+            ((d.n_tok + kRunQuantum - 1) / kRunQuantum) > (int64_t)INT32_MAX)
+        return no("problem too large for one launch");
+
+    if (select_path(d) == kPathSimtF32) {
+        if (d.d_state % 8 != 0 || d.d_state > 256) return no("fp32 path needs d_state % 8 == 0 and <= 256");
+        return true;
+    }
+
+    // tcgen05 path.
+    if (!ctx->tc_ready) return no("tensor-core kernels unavailable on this device");
+    if (d.d_state != 128) return no("bf16 tensor-core path needs d_state == 128");
+    if (d.io_dtype != HELIX_BF16) return no("bf16 tensor-core path needs io_dtype BF16");
+    if (d.s_x[2] != 1) return no("x innermost stride must be 1 for TMA");
+    // TMA: every non-innermost global stride must be a multiple of 16 bytes.
+    const int64_t tma[] = {d.s_x[0], d.s_x[1], d.seq_x, d.s_b[0], d.s_b[1], d.seq_b,
+                           d.s_c[0], d.s_c[1], d.seq_c};
+    for (int64_t s : tma)
+        if (s <= 0 || (s * 2) % 16 != 0) return no("x/B/C strides must be positive multiples of 16 bytes");
+    return true;
+}
+
+Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
+    Plan pl;
+    pl.path = select_path(d);
+    pl.cs = pl.path == kPathTcBf16 ? 128 : (d.d_state <= 128 ? 64 : 32);
+    pl.n_pslab = (d.head_dim + kSlab - 1) / kSlab;
+
+    const int blocks = (d.n_tok + kRunQuantum - 1) / kRunQuantum;  // 128-token blocks
+    int n_runs = 1;
+    if (d.multipass) {
+        // Enough CTAs in the output kernel to cover every SM a few times.
+        const int64_t units = (int64_t)d.n_seq * d.n_head * pl.n_pslab;
+        const int64_t target = 4 * (int64_t)(ctx ? std::max(ctx->n_sm, 1) : 148);
+        n_runs = (int)std::min<int64_t>(blocks, std::max<int64_t>(1, (target + units - 1) / units));
+        const size_t per_run = (size_t)d.n_seq * d.n_head * d.head_dim * d.d_state * sizeof(float);
+        const size_t cap = std::max<size_t>(1, scratch_budget() / std::max<size_t>(per_run, 1));
+        n_runs = (int)std::min<size_t>((size_t)n_runs, cap);
+    }
+    int run_blocks = (blocks + n_runs - 1) / n_runs;
+    if (d.multipass) {
+        if (const int f = forced_run_tokens()) run_blocks = std::max(1, f / kRunQuantum);
+    }
+    pl.run_tok = run_blocks * kRunQuantum;
+    pl.n_runs = (blocks + run_blocks - 1) / run_blocks;
+    pl.need_state_kernel = pl.n_runs > 1;
+
+    if (pl.n_runs > 1) {
+        const size_t agg = (size_t)d.n_seq * d.n_head * pl.n_runs * d.head_dim * d.d_state;
+        const size_t lam = (size_t)d.n_seq * d.n_head * pl.n_runs;
+        pl.off_agg = 0;
+        pl.off_lam = align256(agg * sizeof(float));
+        pl.total = pl.off_lam + align256(lam * sizeof(float));
+    }
+    return pl;
+}
+
+}  // namespace hx
+
+extern "C" bool helix_scan_supported(helix_ctx* ctx, const helix_scan_desc* d) {
+    if (!ctx || !d) return false;
+    std::string why;
+    const bool ok = hx::supported_impl(ctx, *d, &why);
+    if (!ok) hx::set_error(ctx, why);
+    return ok;
+}
+
+extern "C" size_t helix_scan_scratch_size(helix_ctx* ctx, const helix_scan_desc* d) {
+    if (!d || !d->multipass) return 0;
+    return hx::make_plan(ctx, *d).total;
+}
+
+extern "C" helix_backend helix_ctx_select_backend(helix_ctx* ctx, const helix_scan_desc* d) {
+    if (!ctx || !d) return HELIX_BACKEND_REF;
+    if (d->backend == HELIX_BACKEND_REF) return HELIX_BACKEND_REF;
+    return hx::select_path(*d) == hx::kPathTcBf16 ? HELIX_BACKEND_MPP : HELIX_BACKEND_SGMMA;
+}
+
+extern "C" const char* helix_ctx_backend_desc(helix_ctx* ctx, const helix_scan_desc* d) {
+    if (!ctx || !d) return "unavailable (null context)";
+    if (!hx::supported_impl(ctx, *d, nullptr)) return "declined (shape unsupported)";
+    return hx::select_path(*d) == hx::kPathTcBf16
+               ? "tcgen05 (bf16 operands, fp32 accumulators and state)"
+               : "cuda-core (fp32)";
+}

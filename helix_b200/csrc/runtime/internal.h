@@ -1,0 +1,109 @@
+// internal.h -- runtime internals shared by the C++ runtime and the CUDA
+// kernels.  Not installed, not part of the ABI.
+//
+// Replaces the reference's Objective-C++ runtime internals
+// (src/runtime/helix_internal.h:12-110) and its shared Metal parameter block
+// (src/kernels/helix_params.h:45-110).  Differences that matter:
+//   * every stride is 64-bit: config 5 (n_seq=8, L=131072, H=128, P=64) puts
+//     n_seq*seq_x at 8.6e9, beyond the int32 fields the reference validates
+//     against (src/runtime/caps.mm:243-257);
+//   * the sequence is cut into "runs" of whole 128-token blocks.  The state
+//     kernel reduces each run to one fp32 state (its contribution from a zero
+//     start) plus one log-decay; the output kernel rebuilds the state entering
+//     its run from those and walks the run's chunks.  Scratch therefore holds
+//     one state per run instead of the reference's one state per chunk
+//     (src/kernels/helix_params.h:101-109).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "helix/helix.h"
+
+namespace hx {
+
+// Token granularity of runs.  Both kernel families cut runs on this boundary
+// so the scratch plan does not depend on which family runs.
+constexpr int kRunQuantum = 128;
+// Head-dim slab handled by one CTA (reference HELIX_HD, helix_params.h:19).
+constexpr int kSlab = 64;
+
+enum Path : int {
+    kPathSimtF32 = 0,   // exact fp32 CUDA-core kernels
+    kPathTcBf16  = 1,   // tcgen05 kernels, bf16 operands, fp32 state
+};
+
+// How one descriptor is executed.  A pure function of (ctx, desc, env):
+// helix_scan_scratch_size() and the encoder both call make_plan().
+struct Plan {
+    Path   path     = kPathSimtF32;
+    int    cs       = 64;   // chunk length inside the output kernel
+    int    run_tok  = 0;    // tokens per run (multiple of kRunQuantum)
+    int    n_runs   = 1;
+    int    n_pslab  = 1;
+    bool   need_state_kernel = false;  // n_runs > 1
+    size_t off_agg  = 0;    // f32 [seq][head][run][head_dim][d_state]
+    size_t off_lam  = 0;    // f32 [seq][head][run]
+    size_t total    = 0;    // scratch bytes
+};
+
+// Kernel parameter block (passed by value).
+struct ScanParams {
+    int32_t S, L, H, P, N, G, hpg;
+    int32_t n_pslab, run_tok, n_runs;
+    int32_t has_ids;
+    int32_t io_bf16;        // x, B, C stored as bf16
+    float   dt_min, dt_max;
+
+    int64_t s_x0, s_x1, s_x2, seq_x;
+    int64_t s_b0, s_b1, seq_b;        // innermost B stride is 1
+    int64_t s_c0, s_c1, seq_c;        // innermost C stride is 1
+    int64_t s_dt0, s_dt1, seq_dt;
+    int64_t s_s0, s_s1, seq_s;        // innermost state stride is 1
+    int64_t s_y0, s_y1, s_y2, seq_y;
+    int64_t s_a;
+
+    const void*    x;
+    const float*   dt;
+    const float*   A;
+    const void*    B;
+    const void*    C;
+    const int32_t* ids;
+    const float*   s0;
+    float*         y;
+    float*         s1;
+    float*         agg;     // scratch, see Plan
+    float*         lam;
+};
+
+}  // namespace hx
+
+struct helix_ctx {
+    int    device      = 0;
+    int    n_sm        = 0;
+    int    cc_major    = 0;
+    int    cc_minor    = 0;
+    size_t max_smem_optin = 0;
+    bool   tc_ready    = false;   // tensor-core kernels configured
+    void*  encode_tiled = nullptr; // cuTensorMapEncodeTiled entry point
+};
+
+namespace hx {
+
+// Per-thread, per-context last error (helix_ctx_last_error).
+void        set_error(const helix_ctx* ctx, const std::string& msg);
+const char* get_error(const helix_ctx* ctx);
+
+// caps.cpp
+bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why);
+Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d);
+Path select_path(const helix_scan_desc& d);
+
+// Kernel launchers (kernels/*.cu).  Return cudaSuccess or the launch error.
+int launch_simt(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+int configure_simt(const helix_ctx* ctx);
+int configure_tc(const helix_ctx* ctx);
+
+}  // namespace hx

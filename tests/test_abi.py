@@ -1,0 +1,69 @@
+"""CPU: the C-ABI library loads, exports every symbol include/helix/helix.h
+declares, and its host-only behaviour matches the reference's."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from helix_b200 import abi
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    out = []
+    for hdr in sorted((ROOT / "include").rglob("*.h")):
+        txt = re.sub(r"/\*.*?\*/", "", hdr.read_text(), flags=re.S)
+        out += re.findall(r"\b(helix_\w+)\s*\(", txt)
+    inline = {"helix_tensor_is_null"}
+    return sorted(set(out) - inline)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = abi.load()
+    syms = declared_symbols()
+    assert set(abi.EXPORTS) <= set(syms)
+    for s in syms:
+        assert hasattr(lib, s), s
+
+
+def test_struct_layout_matches_reference(reference):
+    assert C.sizeof(abi.ScanDesc) == reference.desc_size()
+
+
+@pytest.mark.parametrize("shape", [(512, 1, 64, 64, 128, 8), (1000, 4, 32, 192, 128, 1), (1, 3, 2, 8, 16, 2)])
+def test_desc_init_matches_reference(reference, shape):
+    ours = abi.desc_init(*shape)
+    theirs = reference.desc_init(*shape)
+    assert bytes(ours) == bytes(theirs)
+
+
+def test_null_handling_without_device():
+    lib = abi.load()
+    d = abi.desc_init(64, 1, 2, 64, 128, 1)
+    assert lib.helix_scan_supported(None, C.byref(d)) is False
+    assert lib.helix_ctx_backend_desc(None, C.byref(d)) == b"unavailable (null context)"
+    assert lib.helix_ctx_select_backend(None, C.byref(d)) == abi.HELIX_BACKEND_REF
+    assert lib.helix_ctx_last_error(None)
+    # single pass needs no scratch, whatever the context
+    assert lib.helix_scan_scratch_size(None, C.byref(d)) == 0
+    st = lib.helix_scan_encode(None, None, C.byref(d), *([abi.NULL_TENSOR] * 10))
+    assert st == abi.HELIX_ERR_INVALID_ARG
+    assert lib.helix_ctx_create(None, None, None) == abi.HELIX_ERR_INVALID_ARG
+
+
+def test_ctx_create_reports_no_device_here():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    lib = abi.load()
+    h = C.c_void_p()
+    assert lib.helix_ctx_create(C.byref(h), None, None) == abi.HELIX_ERR_NO_DEVICE
+    assert not h.value
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(RuntimeError):
+        abi.load(tmp_path / "libhelix.so")
