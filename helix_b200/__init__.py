@@ -74,7 +74,8 @@ class Context:
         None for torch's current stream).  Returns the helix_status."""
         if stream is None:
             import torch
-            stream = torch.cuda.current_stream(x.device)
+            dev = next((t.device for t in (x, y, s0) if t is not None), None)
+            stream = torch.cuda.current_stream(dev)
         handle = getattr(stream, "cuda_stream", stream)
         fn = self.lib.helix_scan_encode_into if into else self.lib.helix_scan_encode
         return int(fn(self.handle, C.c_void_p(handle), C.byref(d), _t(s0), _t(x), _t(dt), _t(A),

@@ -59,11 +59,13 @@ class Tensor(C.Structure):
 
 NULL_TENSOR = Tensor(None, 0)
 
-# Every entry point include/helix/helix.h declares.
+# Every entry point include/helix/*.h declares.
 EXPORTS = (
     "helix_scan_desc_init", "helix_ctx_create", "helix_ctx_free", "helix_ctx_last_error",
     "helix_ctx_select_backend", "helix_ctx_backend_desc", "helix_scan_supported",
     "helix_scan_scratch_size", "helix_scan_encode", "helix_scan_encode_into",
+    # include/helix/helix_ext.h
+    "helix_device_fault",
 )
 
 _lib = None
@@ -100,6 +102,8 @@ def load(path: Path | str | None = None) -> C.CDLL:
     lib.helix_scan_encode.restype = C.c_int
     lib.helix_scan_encode_into.argtypes = enc
     lib.helix_scan_encode_into.restype = C.c_int
+    lib.helix_device_fault.argtypes = [C.c_void_p, P(C.c_uint32)]
+    lib.helix_device_fault.restype = C.c_int
     if path is None:
         _lib = lib
     return lib

@@ -197,6 +197,9 @@ __global__ void __launch_bounds__(kThreads, 1) simt_out_kernel(ScanParams p) {
             const int c = i / NMAX, n = i - c * NMAX;
             Ss[n * kXs + c] = (c < pw && n < N) ? s0[(int64_t)c * p.s_s1 + n] : 0.0f;
         }
+        // The carry loop below maps threads to (c, n) differently when
+        // N < NMAX, so the fill must be complete first.
+        __syncthreads();
         const int64_t unit0 = ((int64_t)tl.seq * p.H + tl.h) * p.n_runs;
         for (int r = 0; r < tl.run; ++r) {
             const float a = expf(p.lam[unit0 + r]);

@@ -9,6 +9,7 @@
 #include <mutex>
 #include <string>
 
+#include "helix/helix_ext.h"
 #include "internal.h"
 
 namespace hx {
@@ -117,4 +118,17 @@ extern "C" const char* helix_ctx_last_error(const helix_ctx* ctx) {
         return *e ? e : "null context";
     }
     return hx::get_error(ctx);
+}
+
+extern "C" helix_status helix_device_fault(helix_ctx* ctx, uint32_t* code) {
+    if (!ctx || !code) return HELIX_ERR_INVALID_ARG;
+    DeviceGuard g(ctx->device);
+    unsigned v = 0;
+    if (hx::read_tc_fault(&v) != cudaSuccess) {
+        hx::set_error(ctx, std::string("reading the fault word failed: ") +
+                               cudaGetErrorString(cudaGetLastError()));
+        return HELIX_ERR_PIPELINE;
+    }
+    *code = v;
+    return HELIX_OK;
 }

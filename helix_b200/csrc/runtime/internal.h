@@ -105,5 +105,6 @@ int launch_simt(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void*
 int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 int configure_simt(const helix_ctx* ctx);
 int configure_tc(const helix_ctx* ctx);
+int read_tc_fault(unsigned* code);
 
 }  // namespace hx

@@ -1,0 +1,105 @@
+"""GPU parity of the tcgen05 kernels (x, B, C stored bf16; bf16 GEMM operands,
+fp32 accumulators and fp32 carried state) against the fp64 oracle run on the
+same bf16-rounded inputs, through the C ABI.
+
+Bounds: y is held to the reference's calibrated bf16 per-element bound
+(reference tests/test_metal_parity.mm:35-38, rel 1.5e-2 / abs 3e-3) and to the
+north star's 2e-2 relative L2.  The carried state is held to a bound 4x the
+fp32 one: the state update multiplies exact bf16 B by dt*decay*x split into a
+bf16 hi+lo pair (~16 mantissa bits), so the carry never passes through a
+single bf16 rounding (the reference's bf16 path keeps its carry fp32 too,
+test_metal_parity.mm:214-218)."""
+import os
+
+import numpy as np
+import pytest
+
+from gpu_harness import BF16_ABS, BF16_REL, BF16_RL2, record, run, widen
+from helpers import compare
+from helix_b200 import abi
+
+pytestmark = pytest.mark.gpu
+
+S1_REL, S1_ABS, S1_RL2 = 2e-5, 2e-6, 1e-4
+
+SHAPES = [  # reference tests/test_metal_parity.mm:77-104, d_state = 128 rows
+    (1, 1, 2, 64, 128, 1), (7, 1, 2, 64, 128, 1), (63, 1, 2, 64, 128, 1),
+    (64, 1, 2, 64, 128, 1), (65, 1, 2, 64, 128, 1), (127, 1, 2, 64, 128, 1),
+    (128, 1, 2, 64, 128, 1), (129, 1, 2, 64, 128, 1), (96, 1, 4, 64, 128, 1),
+    (160, 1, 4, 64, 128, 1), (300, 1, 8, 64, 128, 2), (256, 1, 4, 128, 128, 1),
+    (256, 1, 4, 192, 128, 1), (256, 1, 8, 128, 128, 8), (256, 4, 4, 64, 128, 1),
+    (1024, 1, 2, 64, 128, 1), (2048, 1, 8, 64, 128, 2), (200, 1, 2, 72, 128, 1),
+]
+MODES = [("1pass", False, None), ("multipass", True, None), ("multipass/runs128", True, "128")]
+
+
+@pytest.fixture
+def run_tokens():
+    old = os.environ.get("HELIX_RUN_TOKENS")
+
+    def set_(v):
+        if v is None:
+            os.environ.pop("HELIX_RUN_TOKENS", None)
+        else:
+            os.environ["HELIX_RUN_TOKENS"] = v
+    yield set_
+    set_(old)
+
+
+def check_bf16(tag, y, s1, y_ref, s_ref):
+    cy = compare(y, y_ref, BF16_REL, BF16_ABS)
+    cs = compare(s1, s_ref, S1_REL, S1_ABS)
+    record(tag, y_ratio=cy["ratio"], y_rl2=cy["rel_l2"], s_ratio=cs["ratio"], s_rl2=cs["rel_l2"])
+    assert cy["ok"] and cy["rel_l2"] <= BF16_RL2, (tag, "y", cy)
+    assert cs["ok"] and cs["rel_l2"] <= S1_RL2, (tag, "s1", cs)
+
+
+def _oracle(oracle, prob, shape, ids=None, threads=1):
+    L, S, H, P, N, G = shape
+    d = oracle.desc_init(L, S, H, P, N, G)
+    args = [prob[k] for k in ("s0", "x", "dt", "A", "B", "C")]
+    if threads > 1:
+        return oracle.scan_mt(d, *args, ids=ids, threads=threads)
+    return oracle.scan(d, *args, ids=ids)
+
+
+@pytest.mark.parametrize("long_mem", [False, True], ids=["short", "long"])
+@pytest.mark.parametrize("mode", MODES, ids=[m[0] for m in MODES])
+@pytest.mark.parametrize("shape", SHAPES, ids=["L{}S{}H{}P{}N{}G{}".format(*s) for s in SHAPES])
+def test_parity_bf16(ctx, oracle, run_tokens, shape, mode, long_mem):
+    name, multipass, rt = mode
+    prob = widen(oracle.harness_problem(*shape, 4242, long_mem), "bf16")
+    y_ref, s_ref = _oracle(oracle, prob, shape)
+    run_tokens(rt)
+    y, s1, d = run(ctx, prob, multipass=multipass, io="bf16", compute="bf16")
+    assert ctx.select_backend(d) == abi.HELIX_BACKEND_MPP
+    assert "tcgen05" in ctx.backend_desc(d)
+    check_bf16(f"bf16 {name} {'long' if long_mem else 'short'} {shape}", y, s1, y_ref, s_ref)
+
+
+def test_ids_and_batched_bf16(ctx, oracle, run_tokens):
+    shape = (300, 3, 4, 64, 128, 2)
+    prob = widen(oracle.harness_problem(*shape, 777, True), "bf16")
+    ids = np.array([2, 0, 1], np.int32)
+    y_ref, s_ref = _oracle(oracle, prob, shape, ids=ids)
+    run_tokens("128")
+    y, s1, _ = run(ctx, prob, multipass=True, io="bf16", compute="bf16", ids=ids)
+    check_bf16("bf16 ids", y, s1, y_ref, s_ref)
+
+
+def test_c3_full_size_bf16(ctx, oracle):
+    """BASELINE config 3 at full size on the BASELINE distributions."""
+    from helix_b200.synth import Shape, make_inputs, to_numpy_f32
+    sh = Shape.of("c3")
+    t = make_inputs(sh, seed=1234, s0_std=0.1)
+    prob = {k: to_numpy_f32(t[k]) for k in ("s0", "x", "dt", "A", "B", "C")}
+    y_ref, s_ref = _oracle(oracle, prob, (sh.L, sh.S, sh.H, sh.P, sh.N, sh.G), threads=os.cpu_count() or 1)
+    y, s1, _ = run(ctx, prob, multipass=True, io="bf16", compute="bf16")
+    check_bf16("bf16 c3", y, s1, y_ref, s_ref)
+
+
+def test_no_device_fault_recorded(ctx):
+    import ctypes as C
+    code = C.c_uint32(123)
+    assert ctx.lib.helix_device_fault(ctx.handle, C.byref(code)) == abi.HELIX_OK
+    assert code.value == 0
