@@ -65,7 +65,7 @@ EXPORTS = (
     "helix_ctx_select_backend", "helix_ctx_backend_desc", "helix_scan_supported",
     "helix_scan_scratch_size", "helix_scan_encode", "helix_scan_encode_into",
     # include/helix/helix_ext.h
-    "helix_device_fault",
+    "helix_device_fault", "helix_scan_encode_static",
 )
 
 _lib = None
@@ -104,6 +104,8 @@ def load(path: Path | str | None = None) -> C.CDLL:
     lib.helix_scan_encode_into.restype = C.c_int
     lib.helix_device_fault.argtypes = [C.c_void_p, P(C.c_uint32)]
     lib.helix_device_fault.restype = C.c_int
+    lib.helix_scan_encode_static.argtypes = [C.c_void_p, C.c_void_p, P(ScanDesc)] + [Tensor] * 9
+    lib.helix_scan_encode_static.restype = C.c_int
     if path is None:
         _lib = lib
     return lib
