@@ -269,7 +269,9 @@ def main():
         ms = timed(step, a.steps)
     total_ms = max_over_ranks(sum(ms))
     ms_per_step = total_ms / a.steps
-    launches = 2 if nbytes > 0 else 1
+    # state + carry + output kernels with runs (tcgen05 family), state + output
+    # (fp32 family), or the output kernel alone (single run)
+    launches = (3 if a.compute == "bf16" else 2) if nbytes > 0 else 1
 
     # ---- per-kernel attribution (same steps, passes split) --------------
     def only(p):
@@ -281,7 +283,8 @@ def main():
                 os.environ.pop("HELIX_ONLY_PASS", None)
         return f
     ms_c = max_over_ranks(sum(timed(only("C"), a.steps))) / a.steps
-    ms_a = max_over_ranks(sum(timed(only("A"), a.steps))) / a.steps if launches == 2 else 0.0
+    ms_a = max_over_ranks(sum(timed(only("A"), a.steps))) / a.steps if launches > 1 else 0.0
+    ms_b = max_over_ranks(sum(timed(only("B"), a.steps))) / a.steps if launches > 2 else 0.0
 
     hbm, tc, peak_kind = peaks()
     e_io = 2 if shape.io == "bf16" else 4
@@ -329,7 +332,7 @@ def main():
                    "compute": a.compute, "runs_plan_scratch_bytes": nbytes,
                    "tflops": tflops, "path_alg_bytes": shape.alg_bytes(), "path_gbs": path_gbs,
                    "path_hbm_frac": path_gbs / hbm,
-                   "kernels_ms": {"state": ms_a, "output": ms_c}},
+                   "kernels_ms": {"state": ms_a, "carry": ms_b, "output": ms_c}},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": None, "kernel": "output kernel",
                      "alg_bytes_per_launch": out_bytes, "peak_kind": peak_kind},

@@ -119,6 +119,7 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     if (d.multipass) {
         if (const int f = forced_run_tokens()) run_blocks = std::max(1, f / kRunQuantum);
     }
+    run_blocks = std::max(run_blocks, (blocks + kMaxRuns - 1) / kMaxRuns);
     pl.run_tok = run_blocks * kRunQuantum;
     pl.n_runs = (blocks + run_blocks - 1) / run_blocks;
     pl.need_state_kernel = pl.n_runs > 1;

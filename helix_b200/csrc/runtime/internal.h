@@ -28,6 +28,9 @@ namespace hx {
 constexpr int kRunQuantum = 128;
 // Head-dim slab handled by one CTA (reference HELIX_HD, helix_params.h:19).
 constexpr int kSlab = 64;
+// Upper bound on runs per sequence (the output kernels stage per-run decays
+// and carry weights in shared memory).
+constexpr int kMaxRuns = 256;
 
 enum Path : int {
     kPathSimtF32 = 0,   // exact fp32 CUDA-core kernels
