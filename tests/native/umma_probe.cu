@@ -6,6 +6,8 @@
 //   mode 2: D[128][64]  = P Q[:, :64]    A K-major (threads), B MN-major (TMA)
 //   mode 3: D[128][64]  = P^T Q[:, :64]  A MN-major, two 64-wide tiles (TMA),
 //                                        B MN-major (threads)
+//   mode 4: D[128][128] = P Q^T    A in TMEM (tcgen05.st: row m in lane m,
+//                                  bf16 pairs per column), B K-major (TMA)
 // Waits are bounded; on timeout the kernel records 1 in *status and returns
 // after freeing its TMEM.
 #include <cuda.h>
@@ -73,6 +75,7 @@ __global__ void __launch_bounds__(128, 1) probe_kernel(int mode, const __grid_co
 
     uint32_t tx_bytes = 0;
     if (mode == 0) tx_bytes = 65536;
+    if (mode == 4) tx_bytes = 32768;
     if (mode == 2) tx_bytes = 16384;
     if (mode == 3) tx_bytes = 32768;
     if (tid == 0 && tx_bytes) {
@@ -87,7 +90,24 @@ __global__ void __launch_bounds__(128, 1) probe_kernel(int mode, const __grid_co
         } else if (mode == 3) {
             tma_load_4d(a0, &maps.p, &bar_tma, 0, 0, 0, 0);
             tma_load_4d(a1, &maps.p, &bar_tma, 64, 0, 0, 0);
+        } else if (mode == 4) {
+            tma_load_4d(b0, &maps.q, &bar_tma, 0, 0, 0, 0);
+            tma_load_4d(b1, &maps.q, &bar_tma, 64, 0, 0, 0);
         }
+    }
+    if (mode == 4) {
+        // A = P into TMEM columns 128..191: this thread's row, 64 columns of
+        // packed pairs (P[r][2c] low half, P[r][2c+1] high half).
+        const int r = 32 * (warp & 3) + (tid & 31);
+        for (int c0 = 0; c0 < 64; c0 += 16) {
+            uint32_t w[16];
+            for (int c = 0; c < 16; ++c)
+                w[c] = pack_bf16x2(__bfloat162float(P[r * 128 + 2 * (c0 + c)]),
+                                   __bfloat162float(P[r * 128 + 2 * (c0 + c) + 1]));
+            tmem_st16(tm + ((uint32_t)(32 * (warp & 3)) << 16) + 128 + c0, w);
+        }
+        tmem_wait_st();
+        tc_fence_before();
     }
     if (mode == 1) {
         write_tile(a0, P, 128, 0, false);
@@ -105,7 +125,7 @@ __global__ void __launch_bounds__(128, 1) probe_kernel(int mode, const __grid_co
     if (tx_bytes && !mbar_wait(&bar_tma, 0, 1ll << 31)) abort_flag = 1;
     __syncthreads();
 
-    const int N = (mode <= 1) ? 128 : 64;
+    const int N = (mode <= 1 || mode == 4) ? 128 : 64;
     if (!abort_flag && tid == 0) {
         tc_fence_after();
         const uint32_t sa0 = smem_u32(a0), sb0 = smem_u32(b0);
@@ -121,10 +141,15 @@ __global__ void __launch_bounds__(128, 1) probe_kernel(int mode, const __grid_co
                 ad = sdesc_sw128(sa0 + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
                 bd = sdesc_sw128(sb0 + ks * 2048, 16384, 1024);
                 id = idesc_bf16(128, 64, false, true);
-            } else {  // MN-major A (two tiles along M), MN-major B
+            } else if (mode == 3) {  // MN-major A (two tiles along M), MN-major B
                 ad = sdesc_sw128(sa0 + ks * 2048, 16384, 1024);
                 bd = sdesc_sw128(sb0 + ks * 2048, 16384, 1024);
                 id = idesc_bf16(128, 64, true, true);
+            } else {  // A from TMEM: K step ks = 8 columns
+                bd = sdesc_sw128(sb0 + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+                id = idesc_bf16(128, 128, false, false);
+                mma_bf16_ts(tm, tm + 128 + 8 * ks, bd, id, ks > 0 ? 1u : 0u);
+                continue;
             }
             mma_bf16(tm, ad, bd, id, ks > 0 ? 1u : 0u);
         }
