@@ -14,7 +14,7 @@ from typing import Optional
 
 from . import abi
 
-__all__ = ["HelixError", "Context", "desc_from_tensors", "scan", "abi"]
+__all__ = ["HelixError", "Context", "desc_from_tensors", "scan", "shard_state", "carry_combine", "abi"]
 
 
 class HelixError(RuntimeError):
@@ -67,6 +67,28 @@ class Context:
 
     def backend_desc(self, d: abi.ScanDesc) -> str:
         return self.lib.helix_ctx_backend_desc(self.handle, C.byref(d)).decode()
+
+    def _stream(self, stream, *tensors):
+        if stream is None:
+            import torch
+            dev = next((t.device for t in tensors if t is not None), None)
+            stream = torch.cuda.current_stream(dev)
+        return C.c_void_p(getattr(stream, "cuda_stream", stream))
+
+    def shard_state_scratch_size(self, d: abi.ScanDesc) -> int:
+        return int(self.lib.helix_scan_shard_state_scratch_size(self.handle, C.byref(d)))
+
+    def encode_shard_state(self, d: abi.ScanDesc, x, dt, A, B, Cm, state, log_decay, scratch,
+                           stream=None) -> int:
+        return int(self.lib.helix_scan_shard_state(
+            self.handle, self._stream(stream, x, state), C.byref(d), _t(x), _t(dt), _t(A), _t(B),
+            _t(Cm), _t(state), _t(log_decay), _t(scratch)))
+
+    def encode_carry_combine(self, d: abi.ScanDesc, s0, states, log_decays, n_prev: int, carry,
+                             ids=None, stream=None) -> int:
+        return int(self.lib.helix_scan_carry_combine(
+            self.handle, self._stream(stream, s0, carry), C.byref(d), _t(s0), _t(ids), _t(states),
+            _t(log_decays), C.c_uint32(n_prev), _t(carry)))
 
     def encode(self, d: abi.ScanDesc, s0, x, dt, A, B, Cm, y, s1, ids=None, scratch=None,
                stream=None, into: bool = False) -> int:
@@ -133,3 +155,62 @@ def scan(x, dt, A, B, Cm, s0, ids=None, *, multipass: bool = True, compute: str 
     if st != abi.HELIX_OK:
         raise HelixError(st, ctx.last_error())
     return y, s1
+
+
+def _ctx_for(x, ctx):
+    import torch
+    dev = x.device.index if x.device.index is not None else torch.cuda.current_device()
+    if ctx is None:
+        ctx = _default_ctx.get(dev) or _default_ctx.setdefault(dev, Context(dev))
+    return ctx
+
+
+def shard_state(x, dt, A, B, Cm, *, compute: str = "auto", backend: int = abi.HELIX_BACKEND_AUTO,
+                ctx: Optional[Context] = None, stream=None):
+    """State this token shard leaves from a zero start, and its log-decay.
+
+    x (S, L, H, P), dt (S, L, H), B and Cm (S, L, G, N) hold tokens
+    [l0, l1) of every sequence.  Returns (state (S, H, P, N) f32,
+    log_decay (S, H) f32 = sum_t A_h dt_t).  See helix_ext.h."""
+    import torch
+    ctx = _ctx_for(x, ctx)
+    S, L, H, P = x.shape
+    N = B.shape[3]
+    state = torch.empty((S, H, P, N), dtype=torch.float32, device=x.device)
+    log_decay = torch.empty((S, H), dtype=torch.float32, device=x.device)
+    d = desc_from_tensors(x, dt, B, state, None, multipass=True, compute=compute, backend=backend)
+    if Cm.stride() != B.stride():
+        d.s_c[:] = list(Cm.stride()[1:]); d.seq_c = Cm.stride(0)
+    nbytes = ctx.shard_state_scratch_size(d)
+    scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    st = ctx.encode_shard_state(d, x, dt, A, B, Cm, state, log_decay, scratch, stream=stream)
+    if stream is not None and hasattr(stream, "cuda_stream"):
+        scratch.record_stream(stream)
+    if st != abi.HELIX_OK:
+        raise HelixError(st, ctx.last_error())
+    return state, log_decay
+
+
+def carry_combine(s0, states, log_decays, ids=None, *, ctx: Optional[Context] = None, stream=None):
+    """State entering a shard: fold of S <- exp(log_decays[j]) S + states[j]
+    over the earlier shards j = 0..n-1, from s0[ids[seq]].
+
+    s0 (S0, H, P, N); states (n, S, H, P, N) and log_decays (n, S, H)
+    contiguous f32.  Returns carry (S, H, P, N) f32."""
+    import torch
+    ctx = _ctx_for(s0, ctx)
+    n = int(states.shape[0])
+    S = int(ids.shape[0]) if ids is not None else int(s0.shape[0])
+    H, P, N = s0.shape[1:]
+    carry = torch.empty((S, H, P, N), dtype=torch.float32, device=s0.device)
+    d = abi.desc_init(1, S, H, P, N, 1)
+    d.s_s[:] = list(s0.stride()[1:]); d.seq_s = s0.stride(0)
+    if tuple(carry.stride()) != tuple(s0.stride()):
+        raise ValueError("s0 must be a dense (S, H, P, N) tensor")
+    if n and (not states.is_contiguous() or not log_decays.is_contiguous()):
+        raise ValueError("states and log_decays must be contiguous")
+    st = ctx.encode_carry_combine(d, s0, states if n else None, log_decays if n else None, n, carry,
+                                  ids=ids, stream=stream)
+    if st != abi.HELIX_OK:
+        raise HelixError(st, ctx.last_error())
+    return carry

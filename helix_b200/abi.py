@@ -66,6 +66,7 @@ EXPORTS = (
     "helix_scan_scratch_size", "helix_scan_encode", "helix_scan_encode_into",
     # include/helix/helix_ext.h
     "helix_device_fault", "helix_scan_encode_static",
+    "helix_scan_shard_state_scratch_size", "helix_scan_shard_state", "helix_scan_carry_combine",
 )
 
 _lib = None
@@ -106,6 +107,13 @@ def load(path: Path | str | None = None) -> C.CDLL:
     lib.helix_device_fault.restype = C.c_int
     lib.helix_scan_encode_static.argtypes = [C.c_void_p, C.c_void_p, P(ScanDesc)] + [Tensor] * 9
     lib.helix_scan_encode_static.restype = C.c_int
+    lib.helix_scan_shard_state_scratch_size.argtypes = [C.c_void_p, P(ScanDesc)]
+    lib.helix_scan_shard_state_scratch_size.restype = C.c_size_t
+    lib.helix_scan_shard_state.argtypes = [C.c_void_p, C.c_void_p, P(ScanDesc)] + [Tensor] * 8
+    lib.helix_scan_shard_state.restype = C.c_int
+    lib.helix_scan_carry_combine.argtypes = [C.c_void_p, C.c_void_p, P(ScanDesc)] + [Tensor] * 4 + [
+        C.c_uint32, Tensor]
+    lib.helix_scan_carry_combine.restype = C.c_int
     if path is None:
         _lib = lib
     return lib

@@ -405,6 +405,22 @@ int launch_simt_t(const Plan& pl, const ScanParams& p, int n_seq, cudaStream_t s
 }
 }  // namespace
 
+template <int CS, int NMAX, bool BF16>
+int launch_simt_states_t(const Plan& pl, const ScanParams& p, cudaStream_t st) {
+    using SM = SimtSmem<CS, NMAX>;
+    const int64_t per_run = (int64_t)p.n_pslab * p.H;
+    simt_state_kernel<CS, NMAX, BF16>
+        <<<(unsigned)(per_run * pl.n_runs * p.S), kThreads, SM::state_bytes, st>>>(p, pl.n_runs);
+    return cudaGetLastError();
+}
+
+int launch_simt_states(const helix_ctx*, const Plan& pl, const ScanParams& p, void* stream) {
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (p.N <= 128)
+        return p.io_bf16 ? launch_simt_states_t<64, 128, true>(pl, p, st) : launch_simt_states_t<64, 128, false>(pl, p, st);
+    return p.io_bf16 ? launch_simt_states_t<32, 256, true>(pl, p, st) : launch_simt_states_t<32, 256, false>(pl, p, st);
+}
+
 int launch_simt(const helix_ctx*, const Plan& pl, const ScanParams& p, void* stream) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int n_seq = p.S;

@@ -1600,6 +1600,21 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* s
     return cudaSuccess;
 }
 
+int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream) {
+    auto fn = reinterpret_cast<EncodeFn>(ctx->encode_tiled);
+    if (!fn) return cudaErrorNotSupported;
+    TcMaps maps;
+    const int64_t S = p.S;
+    if (!make_map(fn, &maps.x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x) ||
+        !make_map(fn, &maps.b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b) ||
+        !make_map(fn, &maps.c, p.C, p.N, p.G, p.L, S, p.s_c1, p.s_c0, p.seq_c))
+        return cudaErrorInvalidValue;
+    const int64_t per_run = (int64_t)p.n_pslab * p.H * S;
+    tc_state_kernel<<<(unsigned)(per_run * pl.n_runs), kStThreads, SMEM_STATE, static_cast<cudaStream_t>(stream)>>>(
+        maps, p, pl.n_runs);
+    return cudaGetLastError();
+}
+
 int read_tc_fault(unsigned* code) {
     unsigned v = 0, zero = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_fault, sizeof(v));

@@ -73,7 +73,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long l
 }
 
 // ---------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA: every copy targets this CTA only (no cluster-wide copies anywhere in this library)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
                                             int c1, int c2, int c3) {

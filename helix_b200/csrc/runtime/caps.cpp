@@ -134,6 +134,20 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     return pl;
 }
 
+Plan make_shard_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
+    helix_scan_desc m = d;
+    m.multipass = true;
+    Plan pl = make_plan(ctx, m);
+    if (pl.total == 0) {  // a single run: make_plan keeps no slots for it
+        const size_t agg = (size_t)d.n_seq * d.n_head * pl.n_runs * d.head_dim * d.d_state;
+        const size_t lam = (size_t)d.n_seq * d.n_head * pl.n_runs;
+        pl.off_agg = 0;
+        pl.off_lam = align256(agg * sizeof(float));
+        pl.total = pl.off_lam + align256(lam * sizeof(float));
+    }
+    return pl;
+}
+
 }  // namespace hx
 
 extern "C" bool helix_scan_supported(helix_ctx* ctx, const helix_scan_desc* d) {

@@ -95,27 +95,8 @@ helix_status encode_core(helix_ctx* ctx, void* stream, const helix_scan_desc* d,
     }
 
     hx::ScanParams p{};
-    p.S = d->n_seq;
-    p.L = d->n_tok;
-    p.H = d->n_head;
-    p.P = d->head_dim;
-    p.N = d->d_state;
-    p.G = d->n_group;
-    p.hpg = d->n_head / d->n_group;
-    p.n_pslab = pl.n_pslab;
-    p.run_tok = pl.run_tok;
-    p.n_runs = pl.n_runs;
+    hx::fill_params(p, *d, pl);
     p.has_ids = ids.buf ? 1 : 0;
-    p.io_bf16 = d->io_dtype == HELIX_BF16 ? 1 : 0;
-    p.dt_min = d->dt_min;
-    p.dt_max = d->dt_max;
-    p.s_x0 = d->s_x[0]; p.s_x1 = d->s_x[1]; p.s_x2 = d->s_x[2]; p.seq_x = d->seq_x;
-    p.s_b0 = d->s_b[0]; p.s_b1 = d->s_b[1]; p.seq_b = d->seq_b;
-    p.s_c0 = d->s_c[0]; p.s_c1 = d->s_c[1]; p.seq_c = d->seq_c;
-    p.s_dt0 = d->s_dt[0]; p.s_dt1 = d->s_dt[1]; p.seq_dt = d->seq_dt;
-    p.s_s0 = d->s_s[0]; p.s_s1 = d->s_s[1]; p.seq_s = d->seq_s;
-    p.s_y0 = d->s_y[0]; p.s_y1 = d->s_y[1]; p.s_y2 = d->s_y[2]; p.seq_y = d->seq_y;
-    p.s_a = d->s_a;
     p.x = at<void>(x);
     p.dt = at<float>(dt);
     p.A = at<float>(A);
@@ -155,6 +136,33 @@ helix_status encode_core(helix_ctx* ctx, void* stream, const helix_scan_desc* d,
 }
 
 }  // namespace
+
+namespace hx {
+
+void fill_params(ScanParams& p, const helix_scan_desc& d, const Plan& pl) {
+    p.S = d.n_seq;
+    p.L = d.n_tok;
+    p.H = d.n_head;
+    p.P = d.head_dim;
+    p.N = d.d_state;
+    p.G = d.n_group;
+    p.hpg = d.n_head / d.n_group;
+    p.n_pslab = pl.n_pslab;
+    p.run_tok = pl.run_tok;
+    p.n_runs = pl.n_runs;
+    p.io_bf16 = d.io_dtype == HELIX_BF16 ? 1 : 0;
+    p.dt_min = d.dt_min;
+    p.dt_max = d.dt_max;
+    p.s_x0 = d.s_x[0]; p.s_x1 = d.s_x[1]; p.s_x2 = d.s_x[2]; p.seq_x = d.seq_x;
+    p.s_b0 = d.s_b[0]; p.s_b1 = d.s_b[1]; p.seq_b = d.seq_b;
+    p.s_c0 = d.s_c[0]; p.s_c1 = d.s_c[1]; p.seq_c = d.seq_c;
+    p.s_dt0 = d.s_dt[0]; p.s_dt1 = d.s_dt[1]; p.seq_dt = d.seq_dt;
+    p.s_s0 = d.s_s[0]; p.s_s1 = d.s_s[1]; p.seq_s = d.seq_s;
+    p.s_y0 = d.s_y[0]; p.s_y1 = d.s_y[1]; p.s_y2 = d.s_y[2]; p.seq_y = d.seq_y;
+    p.s_a = d.s_a;
+}
+
+}  // namespace hx
 
 extern "C" helix_status helix_scan_encode(helix_ctx* ctx, void* cmd_buffer,
                                           const helix_scan_desc* d, helix_tensor s0,

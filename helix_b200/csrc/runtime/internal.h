@@ -101,11 +101,30 @@ const char* get_error(const helix_ctx* ctx);
 // caps.cpp
 bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why);
 Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d);
+// Plan of helix_scan_shard_state: the multipass run cut, with one state slot
+// and one log-decay per run for every run (the last one included).
+Plan make_shard_plan(const helix_ctx* ctx, const helix_scan_desc& d);
 Path select_path(const helix_scan_desc& d);
+
+// dispatch.cpp: fills everything but the tensor pointers.
+void fill_params(ScanParams& p, const helix_scan_desc& d, const Plan& pl);
 
 // Kernel launchers (kernels/*.cu).  Return cudaSuccess or the launch error.
 int launch_simt(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+// State kernel over every run of the plan (p.agg / p.lam for all n_runs).
+int launch_simt_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+// kernels/scan_shard.cu
+// state[seq][h] = fold over runs of (exp(lam_r) S + agg_r) from zero, written
+// with the state strides of p (s_s0, s_s1, seq_s); log_decay[seq * H + h] =
+// sum_r lam_r.
+int launch_shard_fold(const ScanParams& p, float* state, float* log_decay, void* stream);
+// carry[seq][h] = fold over j < n_prev of (exp(ld_j) S + states_j) from
+// s0[ids[seq]]; s0 and carry use the state strides of p, states and ld are
+// dense [n_prev][S][H][P][N] and [n_prev][S][H].
+int launch_carry_combine(const ScanParams& p, const float* states, const float* log_decays, int n_prev,
+                         float* carry, void* stream);
 int configure_simt(const helix_ctx* ctx);
 int configure_tc(const helix_ctx* ctx);
 int read_tc_fault(unsigned* code);

@@ -49,6 +49,53 @@ helix_status helix_scan_encode_static(helix_ctx*             ctx,
                                       helix_tensor           y,
                                       helix_tensor           s1);
 
+/* No counterpart in the reference (one Metal device, one encoder).  Support
+ * for cutting every sequence's tokens into contiguous shards, one per GPU
+ * ("L-split"): rank k holds tokens [l_k, l_{k+1}) of x, dt, B and C, with d
+ * describing its shard (d->n_tok = shard length).  Per rank:
+ *
+ *   1. helix_scan_shard_state: the state the shard leaves from a zero start,
+ *      state[seq][h][p][n] = sum_t exp(sum_{t'>t} A_h dt_t') dt_t x_t[p] B_t[n]
+ *      (state strides s_s / seq_s of d, innermost 1), and its log-decay
+ *      log_decay[seq * n_head + h] = sum_t A_h dt_t (natural log; f32).
+ *   2. The caller gathers (state, log_decay) of ranks 0..k-1 (e.g. an
+ *      all-gather over the ranks sharing the same heads) into dense arrays
+ *      states[j][seq][h][p][n] and log_decays[j][seq][h], j = 0..n_prev-1.
+ *   3. helix_scan_carry_combine: carry = the fold over j of
+ *      S <- exp(log_decays[j]) S + states[j], starting from s0[ids[seq]]
+ *      (ids may be null: s0[seq]); carry uses the state strides of d and
+ *      must not overlap s0.
+ *   4. helix_scan_encode on the shard with s0 = carry and ids = null.  The
+ *      last shard's s1 is every sequence's final state.
+ *
+ * helix_scan_shard_state computes in d's precision path (compute_dtype,
+ * backend) and needs helix_scan_shard_state_scratch_size() bytes of
+ * 256-byte-aligned scratch (multipass is implied).  Both are enqueued on
+ * `stream` and never synchronise or allocate. */
+size_t helix_scan_shard_state_scratch_size(helix_ctx* ctx, const helix_scan_desc* d);
+
+helix_status helix_scan_shard_state(helix_ctx*             ctx,
+                                    void*                  stream,
+                                    const helix_scan_desc* d,
+                                    helix_tensor           x,
+                                    helix_tensor           dt,
+                                    helix_tensor           A,
+                                    helix_tensor           B,
+                                    helix_tensor           C,
+                                    helix_tensor           state,
+                                    helix_tensor           log_decay,
+                                    helix_tensor           scratch);
+
+helix_status helix_scan_carry_combine(helix_ctx*             ctx,
+                                      void*                  stream,
+                                      const helix_scan_desc* d,
+                                      helix_tensor           s0,
+                                      helix_tensor           ids,
+                                      helix_tensor           states,
+                                      helix_tensor           log_decays,
+                                      uint32_t               n_prev,
+                                      helix_tensor           carry);
+
 #ifdef __cplusplus
 }
 #endif
