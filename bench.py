@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--cpu-sample-tokens", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--lsplit", type=int, default=0,
+                    help="token shards per head shard: run the L-split mesh on --config (default c5)")
+    ap.add_argument("--seqs", type=int, default=0, help="override the config's sequence count (L-split mode)")
     return ap.parse_args()
 
 
@@ -171,6 +174,105 @@ def peaks():
 
 
 # ---------------------------------------------------------------------------
+def bench_lsplit(a, rank: int, world: int, local: int) -> int:
+    """L-split mesh: world = (world / K head shards) x (K token shards) over
+    the global workload of --config.  A step is one scan_lsplit on every rank
+    (shard state, two all-gathers over the token group, carry combine, shard
+    scan); value = global tokens / max device time over ranks (strong
+    scaling: the global problem is fixed)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import helix_b200
+    from helix_b200 import dist as hdist
+    from helix_b200.synth import Shape, make_inputs
+
+    cfg = a.config if a.config != "c3" else "c5"
+    g = Shape.of(cfg)
+    S = a.seqs or g.S
+    K = a.lsplit
+    if world % K or g.L % (K * 128):
+        raise SystemExit(f"--lsplit {K} does not divide {world} ranks / L={g.L}")
+    n_hs = world // K
+    hs, ls = rank // K, rank % K
+    h0, h1 = hdist.head_slice(g.H, g.G, hs, n_hs)
+    Lk = g.L // K
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    groups = [dist.new_group(list(range(q * K, (q + 1) * K))) for q in range(n_hs)] if world > 1 else [None]
+    grp = groups[hs]
+    local_shape = Shape(S, Lk, h1 - h0, g.P, g.N, (h1 - h0) // (g.H // g.G), g.io)
+    t = make_inputs(local_shape, seed=7000 + rank, device=dev)
+    gA = torch.Generator(device=dev)
+    gA.manual_seed(9000 + hs)
+    t["A"] = -torch.exp(torch.rand(h1 - h0, generator=gA, device=dev) * 2.772588722239781)
+    ops = hdist.GpuOps(compute=a.compute)
+    # per step: state kernel + fold, carry combine, then the shard scan (state,
+    # carry and output kernels with several runs, the output kernel alone with one)
+    d_scan = helix_b200.desc_from_tensors(t["x"], t["dt"], t["B"], t["s0"], None, multipass=True,
+                                          compute=a.compute)
+    ctx = helix_b200._ctx_for(t["x"], None)
+    launches = 3 + ((3 if a.compute == "bf16" else 2) if ctx.scratch_size(d_scan) else 1)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        if world > 1:
+            return hdist.scan_lsplit(t["x"], t["dt"], t["A"], t["B"], t["C"], t["s0"], group=grp, ops=ops)
+        st, ld = ops.shard_state(t["x"], t["dt"], t["A"], t["B"], t["C"])
+        carry = ops.carry_combine(t["s0"], st[None][:0], ld[None][:0], None)
+        return ops.scan(t["x"], t["dt"], t["A"], t["B"], t["C"], carry)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(a.warmup):
+        flush.fill_(1)
+        step()
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    with Clocks(local) as clk:
+        barrier()
+        for e0, e1 in evs:
+            flush.fill_(1)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        barrier()
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / a.steps
+    if world > 1:
+        tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    gshape = Shape(S, g.L, g.H, g.P, g.N, g.G, g.io)
+    value = S * g.L / (ms * 1e-3)
+    hbm, tc, peak_kind = peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "SSD prefill tok/s, L-split mesh (head shards x token shards)", "value": value,
+            "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16" if a.compute == "bf16" else "f32",
+            "data": "synthetic (seeded per rank, BASELINE distributions)",
+            "config": {"workload": f"{cfg}: S={S} L={g.L} H={g.H} P={g.P} N={g.N} G={g.G} as {n_hs} head "
+                                   f"shards x {K} token shards; per rank S={S} L={Lk} H={h1 - h0}",
+                       "l2": "flushed before every timed step (256 MiB write, untimed)",
+                       "step": "shard state + 2 all-gathers + carry combine + shard scan",
+                       "tflops": gshape.flops() / (ms * 1e-3) / 1e12,
+                       "path_gbs": gshape.alg_bytes() / (ms * 1e-3) / 1e9,
+                       "path_hbm_frac_per_gpu": gshape.alg_bytes() / world / (ms * 1e-3) / 1e9 / hbm},
+            "gpu_launches": launches * a.steps, "clocks": clk.summary()}), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -178,6 +280,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
     from helix_b200.synth import Shape
+    if a.lsplit and a.impl != "reference":
+        return bench_lsplit(a, rank, world, local)
     shape = Shape.of(a.config)
 
     if a.impl == "reference":
