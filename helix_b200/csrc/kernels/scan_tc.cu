@@ -1266,10 +1266,13 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
 
 // ---------------------------------------------------------------------------
 // State kernel: the run's state from a zero start, G4 accumulated over the
-// whole run in one TMEM accumulator, plus the run's log-decay.
+// whole run in one TMEM accumulator, plus the run's log-decay.  Sized for two
+// CTAs per SM (98 KB of shared memory, 128 TMEM columns, 320 threads at up to
+// 96 registers): the two CTAs hide each other's load and hand-off latencies.
 //
-//   warps 0-7  (256)  xw hi/lo from x and the decay weights (2 buffers)
-//   warp 8  (lane 0)  TMA producer (3-stage ring of B + x) and MMA issuer
+//   warps 0-7  (256)  x from global (next chunk prefetched in registers),
+//                     xw = w x as bf16 hi | lo into the single xw buffer
+//   warp 8  (lane 0)  TMA producer (B, 2 stages) and MMA issuer
 //   warp 9            decay weights w_j = dt_j exp(sum_{i>j in run} A dt_i)
 //                     into a 4-slot ring, running ahead of the builders
 //
@@ -1278,15 +1281,16 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
 // ---------------------------------------------------------------------------
 constexpr int kStEpi = 256;
 constexpr int kStThreads = kStEpi + 64;
-constexpr int kStStages = 3;
+constexpr int kStStages = 2;
 constexpr int kStRing = 4;
-constexpr uint32_t SO_STAGE = 49152;                   // B 32 KB | x 16 KB
-constexpr uint32_t SO_XW = kStStages * SO_STAGE;       // 2 x (hi 16 KB | lo 16 KB)
-constexpr uint32_t SO_W = SO_XW + 2 * 32768;           // kStRing x 128 weights
+constexpr int kStVec = 1024 / kStEpi;                  // 16-byte x vectors per builder thread
+constexpr uint32_t SO_STAGE = 32768;                   // B: two 64-state tiles
+constexpr uint32_t SO_XW = kStStages * SO_STAGE;       // hi 16 KB | lo 16 KB
+constexpr uint32_t SO_W = SO_XW + 32768;               // kStRing x 128 weights
 constexpr uint32_t SMEM_STATE = SO_W + kStRing * 512 + 1024;
 
 struct StBars {
-    uint64_t full[kStStages], b_done[kStStages], xw_full[2], xw_empty[2], w_full[kStRing], w_empty[kStRing];
+    uint64_t full[kStStages], b_done[kStStages], xw_full, xw_empty, w_full[kStRing], w_empty[kStRing];
 };
 
 __device__ __forceinline__ bool st_wait(uint64_t* bar, uint32_t parity, unsigned code) {
@@ -1296,7 +1300,32 @@ __device__ __forceinline__ bool st_wait(uint64_t* bar, uint32_t parity, unsigned
     return all;
 }
 
-__global__ void __launch_bounds__(kStThreads, 1) tc_state_kernel(const __grid_constant__ TcMaps maps, ScanParams p,
+// x of one chunk for builder thread r: vectors idx = r + kStEpi k (8 channels
+// each); tokens from t_end on and channels from pw on read as zero.
+__device__ __forceinline__ void st_load_x(const ScanParams& p, int64_t xb, int t0, int t_end, int pw, int r,
+                                          uint4 (&v)[kStVec]) {
+    const __nv_bfloat16* xg = static_cast<const __nv_bfloat16*>(p.x);
+#pragma unroll
+    for (int k = 0; k < kStVec; ++k) {
+        const int idx = r + kStEpi * k, j = idx >> 3, c = idx & 7;
+        const int t = t0 + j;
+        v[k] = make_uint4(0u, 0u, 0u, 0u);
+        if (t < t_end) {
+            const __nv_bfloat16* src = xg + xb + (int64_t)t * p.s_x0 + 8 * c;
+            if (8 * c + 8 <= pw) {
+                v[k] = __ldg(reinterpret_cast<const uint4*>(src));
+            } else if (8 * c < pw) {
+                uint16_t e[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) e[q] = 8 * c + q < pw ? __bfloat16_as_ushort(src[q]) : (uint16_t)0;
+                v[k] = make_uint4(e[0] | (uint32_t)e[1] << 16, e[2] | (uint32_t)e[3] << 16, e[4] | (uint32_t)e[5] << 16,
+                                  e[6] | (uint32_t)e[7] << 16);
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_constant__ TcMaps maps, ScanParams p,
                                                                  int runs_in_grid) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
@@ -1321,7 +1350,8 @@ __global__ void __launch_bounds__(kStThreads, 1) tc_state_kernel(const __grid_co
     const int n_ch = (t_end - t_begin + kCS - 1) / kCS;
     const int64_t db = (int64_t)tl.seq * p.seq_dt + (int64_t)tl.h * p.s_dt1;
     auto stage = [&](int q) { return sm + (uint32_t)(q % kStStages) * SO_STAGE; };
-    auto xwbuf = [&](int q) { return sm + SO_XW + (uint32_t)(q & 1) * 32768u; };
+    uint8_t* sXH = sm + SO_XW;
+    uint8_t* sXL = sXH + 16384;
     auto t0_of = [&](int q) { return t_begin + (n_ch - 1 - q) * kCS; };  // visit order q -> chunk
 
     if (tid == 0) {
@@ -1329,10 +1359,8 @@ __global__ void __launch_bounds__(kStThreads, 1) tc_state_kernel(const __grid_co
             mbar_init(&bars.full[k], 1);
             mbar_init(&bars.b_done[k], 1);
         }
-        for (int k = 0; k < 2; ++k) {
-            mbar_init(&bars.xw_full[k], kStEpi / 32);
-            mbar_init(&bars.xw_empty[k], 1);
-        }
+        mbar_init(&bars.xw_full, kStEpi / 32);
+        mbar_init(&bars.xw_empty, 1);
         for (int k = 0; k < kStRing; ++k) {
             mbar_init(&bars.w_full[k], 1);
             mbar_init(&bars.w_empty[k], kStEpi / 32);
@@ -1351,16 +1379,14 @@ __global__ void __launch_bounds__(kStThreads, 1) tc_state_kernel(const __grid_co
         uint8_t* st = stage(q);
         uint64_t* bar = &bars.full[q % kStStages];
         const int t0 = t0_of(q);
-        mbar_expect_tx(bar, 3 * 16384);
+        mbar_expect_tx(bar, 2 * 16384);
         tma_load_4d(st, &maps.b, bar, 0, g, t0, tl.seq);
         tma_load_4d(st + 16384, &maps.b, bar, 64, g, t0, tl.seq);
-        tma_load_4d(st + 32768, &maps.x, bar, p0, tl.h, t0, tl.seq);
     };
 
     bool ok = true;
     if (is_mma) {
         if ((tid & 31) == 0) {
-            prefetch_tmap(&maps.x);
             prefetch_tmap(&maps.b);
             for (int q = 0; q < kStStages && q < n_ch; ++q) load(q);
             HX_PHASE_T(16, 256);
@@ -1369,20 +1395,19 @@ __global__ void __launch_bounds__(kStThreads, 1) tc_state_kernel(const __grid_co
                 const uint32_t pf = (uint32_t)((q / kStStages) & 1);
                 if (!(ok = mbar_wait(&bars.full[s], pf, kWaitBudget))) break;
                 HX_PHASE_T(17, 256);
-                if (!(ok = mbar_wait(&bars.xw_full[q & 1], (uint32_t)((q >> 1) & 1), kWaitBudget))) break;
+                if (!(ok = mbar_wait(&bars.xw_full, (uint32_t)(q & 1), kWaitBudget))) break;
                 HX_PHASE_T(18, 256);
                 tc_fence_after();
                 // one N = 128 MMA per K step: [xw_hi | xw_lo] side by side (16 KB apart)
-                const uint32_t aB = smem_u32(stage(q)), aXW = smem_u32(xwbuf(q));
+                const uint32_t aB = smem_u32(stage(q)), aXW = smem_u32(sXH);
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
                     mma_bf16(tm, desc_mnmajor(aB, ks), desc_mnmajor(aXW, ks), ID_G4W, (q > 0 || ks > 0) ? 1u : 0u);
-                mma_commit(&bars.xw_empty[q & 1]);
+                mma_commit(&bars.xw_empty);
                 mma_commit(&bars.b_done[s]);
                 HX_PHASE_T(19, 256);
                 if (q + kStStages < n_ch) {
-                    // the builders consumed this stage's x before xw_full; B is
-                    // free once these MMAs retire
+                    // B is free once these MMAs retire
                     if (!(ok = mbar_wait(&bars.b_done[s], pf, kWaitBudget))) break;
                     load(q + kStStages);
                 }
@@ -1390,7 +1415,7 @@ __global__ void __launch_bounds__(kStThreads, 1) tc_state_kernel(const __grid_co
             }
             if (!ok) {
                 atomicCAS(&g_tc_fault, 0u, kFaultMmaState);
-                mbar_wait(&bars.xw_empty[0], 0, kWaitBudget);
+                mbar_wait(&bars.xw_empty, 0, kWaitBudget);
             }
         }
         __syncwarp();
@@ -1426,28 +1451,26 @@ __global__ void __launch_bounds__(kStThreads, 1) tc_state_kernel(const __grid_co
     } else {
         // ---- xw builders ----------------------------------------------------
         HX_PHASE(21);
+        const int64_t xb = (int64_t)tl.seq * p.seq_x + (int64_t)tl.h * p.s_x1 + p0;
+        uint4 cur[kStVec], nxt[kStVec];
+        if (n_ch > 0) st_load_x(p, xb, t0_of(0), t_end, pw, tid, cur);
         for (int q = 0; q < n_ch; ++q) {
+            if (q + 1 < n_ch) st_load_x(p, xb, t0_of(q + 1), t_end, pw, tid, nxt);
             const int slot = q % kStRing;
             if (!(ok = st_wait(&bars.w_full[slot], (uint32_t)((q / kStRing) & 1), kFaultMmaState))) break;
             HX_PHASE(22);
-            if (q >= 2) {
-                if (!(ok = st_wait(&bars.xw_empty[q & 1], (uint32_t)(((q - 2) >> 1) & 1), kFaultMmaState))) break;
+            if (q >= 1) {  // the single xw buffer: G4(q-1) retired
+                if (!(ok = st_wait(&bars.xw_empty, (uint32_t)((q - 1) & 1), kFaultMmaState))) break;
             }
             HX_PHASE(23);
-            if (!(ok = st_wait(&bars.full[q % kStStages], (uint32_t)((q / kStStages) & 1), kFaultTmaState))) break;
-            HX_PHASE(24);
             const float* wv = wring + slot * 128;
-            const uint8_t* sX = stage(q) + 32768;
-            uint8_t* sXH = xwbuf(q);
-            uint8_t* sXL = sXH + 16384;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < kStVec; ++k) {
                 const int i = tid + kStEpi * k;
                 const int j = i >> 3, c = i & 7;
                 const uint32_t off = sw128_off(j, c);
-                const uint4 rw = *reinterpret_cast<const uint4*>(sX + off);
                 const float wj = wv[j];
-                const uint32_t in[4] = {rw.x, rw.y, rw.z, rw.w};
+                const uint32_t in[4] = {cur[k].x, cur[k].y, cur[k].z, cur[k].w};
                 uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -1466,14 +1489,15 @@ __global__ void __launch_bounds__(kStThreads, 1) tc_state_kernel(const __grid_co
             fence_async_smem();
             __syncwarp();
             if ((tid & 31) == 0) {
-                mbar_arrive(&bars.xw_full[q & 1]);
+                mbar_arrive(&bars.xw_full);
                 mbar_arrive(&bars.w_empty[slot]);
             }
+#pragma unroll
+            for (int k = 0; k < kStVec; ++k) cur[k] = nxt[k];
             HX_PHASE(25);
         }
         // all G4 MMAs retired: the last chunk's commit
-        if (ok && n_ch > 0)
-            ok = st_wait(&bars.xw_empty[(n_ch - 1) & 1], (uint32_t)(((n_ch - 1) >> 1) & 1), kFaultMmaState);
+        if (ok && n_ch > 0) ok = st_wait(&bars.xw_empty, (uint32_t)((n_ch - 1) & 1), kFaultMmaState);
         tc_fence_after();
         if (ok) {
             const int64_t unit = ((int64_t)tl.seq * p.H + tl.h) * p.n_runs + tl.run;
@@ -1497,7 +1521,10 @@ __global__ void __launch_bounds__(kStThreads, 1) tc_state_kernel(const __grid_co
     __syncthreads();
     if (ok && tid == 0 && tl.slab == 0)
         p.lam[((int64_t)tl.seq * p.H + tl.h) * p.n_runs + tl.run] = lam_total;
-    if (is_mma) tmem_dealloc(tm, 128);
+    if (is_mma) {
+        tc_fence_after();
+        tmem_dealloc(tm, 128);
+    }
     HX_PHASE(26);
 }
 
