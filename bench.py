@@ -399,6 +399,10 @@ def main():
     # y written once, s0 read and s1 written once.
     out_bytes = n_x * e_io + 2 * n_bc * e_io + shape.S * shape.L * shape.H * 4 + n_x * 4 + 2 * n_st * 4
     achieved = out_bytes / (ms_c * 1e-3) / 1e9
+    traffic = None  # DRAM bytes per launch of the output kernel, from the committed ncu capture
+    tj = ROOT / "profiles" / "ncu_traffic.json"
+    if tj.exists() and a.compute == "bf16":
+        traffic = json.loads(tj.read_text()).get(a.config, {}).get("dram_bytes_per_launch")
     path_gbs = shape.alg_bytes() / (ms_per_step * 1e-3) / 1e9
     tflops = shape.flops() / (ms_per_step * 1e-3) / 1e12
 
@@ -438,7 +442,7 @@ def main():
                    "path_hbm_frac": path_gbs / hbm,
                    "kernels_ms": {"state": ms_a, "carry": ms_b, "output": ms_c}},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "traffic": None, "kernel": "output kernel",
+                     "frac": achieved / hbm, "traffic": traffic, "kernel": "output kernel",
                      "alg_bytes_per_launch": out_bytes, "peak_kind": peak_kind},
         "gpu_launches": launches * a.steps,
         "clocks": clk.summary(),

@@ -89,6 +89,12 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
     return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
+// Descriptor of a shared-memory address `off` bytes past the one `base`
+// describes.  Shared addresses stay below 256 KB, so the 14-bit start field
+// never carries into the next field and the offset simply adds.
+__device__ __forceinline__ uint64_t desc_add(uint64_t base, uint32_t off) { return base + (uint64_t)(off >> 4); }
+__device__ __forceinline__ uint32_t kmajor_off(int ks) { return (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u; }
+
 // K-major operand: K step ks (16 elements) of a 2-tile (K = 128) operand.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int ks) {
     return sdesc_sw128(base + (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u, 16, 1024);
@@ -676,12 +682,16 @@ static_assert(OF_V + kFRing * kFVec * 4 + 1024 <= SMEM_OUT, "fast path fits the 
 constexpr uint32_t TF_D4 = 256, TF_D = 320, TF_M = 448;
 constexpr uint32_t ID_G4N = idesc_bf16(128, 64, true, true);
 constexpr float kFastSpan2 = 86.0f;  // ~59.6 nats
-constexpr int kWarpY = 0, kWarpM = 4, kWarpC = 8, kWarpXw = 12, kWarpMma = 18, kWarpVec = 19;
-constexpr int kXwWarps = 6;
+// Warp w runs on SM sub-partition w % 4.  The MMA warp's sub-partition hosts
+// only the light vector warp and one warp of each TMEM role: an ALU-heavy
+// neighbour (the xw builders) slows its MMA issue by about a third.
+constexpr int kWarpY = 0, kWarpM = 4, kWarpC = 8, kWarpXw = 12, kWarpMma = 14, kWarpVec = 18;
+constexpr int kXwWarps = 6;  // warps 12, 13, 15, 16, 17, 19
+__device__ __forceinline__ int xw_index(int warp) { return warp < 14 ? warp - 12 : warp < 18 ? warp - 13 : warp - 14; }
 constexpr int kXwThreads = 32 * kXwWarps;
 constexpr int kXwVec = (1024 + kXwThreads - 1) / kXwThreads;
 constexpr int kMmaTid = 32 * kWarpMma;
-static_assert(kWarpVec + 1 == kOutThreads / 32, "warp roles cover the block");
+static_assert(kOutThreads / 32 == 20, "warp map of the fast path assumes 20 warps");
 
 struct FastBars {
     uint64_t xw_ready[2], xw_free[2], acc1[2], g2[2], d_free[2], m_ready, g4, d4_ready, s_ready, g3;
@@ -793,6 +803,10 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
                 const uint32_t par = (uint32_t)(i & 1);
                 const uint32_t aC = smem_u32(sCB(i)), aB = aC + 32768, aX = smem_u32(sXW(i));
                 const uint32_t tD1 = tm + 128u * (uint32_t)b, tD = tm + TF_D + 64u * (uint32_t)b;
+                // base descriptors; each K step below adds a constant
+                const uint64_t dCk = sdesc_sw128(aC, 16, 1024), dBk = sdesc_sw128(aB, 16, 1024);
+                const uint64_t dBm = sdesc_sw128(aB, 16384, 1024), dXm = sdesc_sw128(aX, 16384, 1024);
+                const uint64_t dSm = sdesc_sw128(aS, 16384, 1024);
                 // D1[b]: W_m(i-2) read it before m_ready(i-2), which G2(i-2) waited for
                 if (!(ok = mbar_wait(&cb_bar[b], bpar(i), kWaitBudget))) break;
                 HX_TL(0, i);
@@ -800,7 +814,7 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16(tD1, desc_kmajor(aC, ks), desc_kmajor(aB, ks), ID_G1, ks > 0);
+                    mma_bf16(tD1, desc_add(dCk, kmajor_off(ks)), desc_add(dBk, kmajor_off(ks)), ID_G1, ks > 0);
                 mma_commit(&bars.acc1[b]);
                 HX_TL(1, i);
                 // G4 accumulates onto S~_i, which W_c left in D4
@@ -811,10 +825,10 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16(tm + TF_D4, desc_mnmajor(aB, ks), desc_mnmajor(aX, ks), ID_G4N, 1u);
+                    mma_bf16(tm + TF_D4, desc_add(dBm, 2048u * ks), desc_add(dXm, 2048u * ks), ID_G4N, 1u);
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16(tm + TF_D4, desc_mnmajor(aB, ks), desc_mnmajor(aX + 16384, ks), ID_G4N, 1u);
+                    mma_bf16(tm + TF_D4, desc_add(dBm, 2048u * ks), desc_add(dXm, 16384u + 2048u * ks), ID_G4N, 1u);
                 mma_commit(&bars.g4);
                 HX_TL(3, i);
                 if (!(ok = mbar_wait(&bars.s_ready, par, kWaitBudget))) break;
@@ -826,7 +840,7 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16(tD, desc_kmajor(aC, ks), desc_mnmajor(aS, ks), ID_G3, ks > 0);
+                    mma_bf16(tD, desc_add(dCk, kmajor_off(ks)), desc_add(dSm, 2048u * ks), ID_G3, ks > 0);
                 mma_commit(&bars.g3);
                 HX_TL(5, i);
                 if (!(ok = mbar_wait(&bars.m_ready, par, kWaitBudget))) break;
@@ -835,7 +849,7 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16_ts(tD, tm + TF_M + 8u * (uint32_t)ks, desc_mnmajor(aX, ks), ID_G2, 1u);
+                    mma_bf16_ts(tD, tm + TF_M + 8u * (uint32_t)ks, desc_add(dXm, 2048u * ks), ID_G2, 1u);
                 mma_commit(&bars.g2[b]);
                 HX_TL(7, i);
                 // G1, G4, G3 of chunk i were the last readers of C/B[b]
@@ -879,7 +893,7 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
         if (!ok) atomicCAS(&g_tc_fault, 0u, kFaultMmaOut);
     } else if (warp >= kWarpXw) {
         // ================= W_xw: xw = w x, hi | lo ===========================
-        const int r = tid - 32 * kWarpXw;
+        const int r = 32 * xw_index(warp) + lane;
         const bool leader = r == 0;
         uint4 cur[kXwVec], nxt[kXwVec];  // chunk 0 was prefetched by the kernel prologue
 #pragma unroll
@@ -893,7 +907,7 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
                 if (!(ok = group_wait(&bars.xw_free[i & 1], bpar(i - 2), 5, kXwThreads, leader))) break;
             }
             if (leader) HX_TL(18, i);
-            HX_PHASE_T(7, 32 * kWarpXw);
+            HX_PHASE_T(7, 32 * 12);
             const float* wv = slot(i);
             uint8_t* xh = sXW(i);
 #pragma unroll
@@ -928,7 +942,7 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
             if (leader) HX_TL(19, i);
 #pragma unroll
             for (int k = 0; k < kXwVec; ++k) cur[k] = nxt[k];
-            HX_PHASE_T(8, 32 * kWarpXw);
+            HX_PHASE_T(8, 32 * 12);
         }
     } else if (warp >= kWarpC) {
         // ================= W_c: the carry, in the G4 accumulator ===========
@@ -1179,9 +1193,9 @@ __global__ void __launch_bounds__(kOutThreads, 1)
         if (lane == 0 && mx > 0.0f) atomicMax(&span_bits, __float_as_uint(mx));
     } else if (warp < kWarpXw) {
         load_state_row(p, ot, 32 * (warp & 3) + lane, pre);
-    } else if (warp < kWarpMma) {
+    } else if (warp != kWarpMma && warp != kWarpVec) {
         uint4 v[kXwVec];
-        load_x_chunk(p, ot, tid - 32 * kWarpXw, 0, v);
+        load_x_chunk(p, ot, 32 * xw_index(warp) + lane, 0, v);
 #pragma unroll
         for (int k = 0; k < kXwVec; ++k) {
             pre[4 * k] = __uint_as_float(v[k].x);
@@ -1267,30 +1281,35 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
 // ---------------------------------------------------------------------------
 // State kernel: the run's state from a zero start, G4 accumulated over the
 // whole run in one TMEM accumulator, plus the run's log-decay.  Sized for two
-// CTAs per SM (98 KB of shared memory, 128 TMEM columns, 320 threads at up to
-// 96 registers): the two CTAs hide each other's load and hand-off latencies.
+// CTAs per SM (107 KB of shared memory, 128 TMEM columns, 320 threads): the
+// two CTAs hide each other's latencies.  It streams in 64-token steps (half
+// chunks), which buys three-deep rings for B and x and two xw buffers within
+// that budget, so no load latency sits on the MMA chain.
 //
-//   warps 0-7  (256)  x from global (next chunk prefetched in registers),
-//                     xw = w x as bf16 hi | lo into the single xw buffer
-//   warp 8  (lane 0)  TMA producer (B, 2 stages) and MMA issuer
+//   warps 0-7  (256)  xw = w x as bf16 hi | lo from the x ring
+//   warp 8  (lane 0)  TMA producer (B and x, 3 stages each) and MMA issuer:
+//                     per step four 128 x 128 x 16 MMAs, A = B (MN-major),
+//                     B = [xw_hi | xw_lo] (MN-major)
 //   warp 9            decay weights w_j = dt_j exp(sum_{i>j in run} A dt_i)
-//                     into a 4-slot ring, running ahead of the builders
+//                     per 128-token chunk into a 4-slot ring
 //
 // Chunks are visited last to first so the decay from token j to the end of
 // the run is a sum of same-sign terms.
 // ---------------------------------------------------------------------------
 constexpr int kStEpi = 256;
 constexpr int kStThreads = kStEpi + 64;
-constexpr int kStStages = 2;
+constexpr int kStHalf = 64;                            // tokens per step
+constexpr int kStStages = 3;
 constexpr int kStRing = 4;
-constexpr int kStVec = 1024 / kStEpi;                  // 16-byte x vectors per builder thread
-constexpr uint32_t SO_STAGE = 32768;                   // B: two 64-state tiles
-constexpr uint32_t SO_XW = kStStages * SO_STAGE;       // hi 16 KB | lo 16 KB
-constexpr uint32_t SO_W = SO_XW + 32768;               // kStRing x 128 weights
+constexpr uint32_t SO_B = 0;                           // 3 x 16 KB: B rows of one step, states 0-63 | 64-127
+constexpr uint32_t SO_X = SO_B + kStStages * 16384;    // 3 x 8 KB: x rows of one step
+constexpr uint32_t SO_XW = SO_X + kStStages * 8192;    // 2 x (hi 8 KB | lo 8 KB)
+constexpr uint32_t SO_W = SO_XW + 2 * 16384;           // kStRing x 128 weights
 constexpr uint32_t SMEM_STATE = SO_W + kStRing * 512 + 1024;
 
 struct StBars {
-    uint64_t full[kStStages], b_done[kStStages], xw_full, xw_empty, w_full[kStRing], w_empty[kStRing];
+    uint64_t b_full[kStStages], b_done[kStStages], x_full[kStStages], xw_full[2], xw_empty[2];
+    uint64_t w_full[kStRing], w_empty[kStRing];
 };
 
 __device__ __forceinline__ bool st_wait(uint64_t* bar, uint32_t parity, unsigned code) {
@@ -1298,31 +1317,6 @@ __device__ __forceinline__ bool st_wait(uint64_t* bar, uint32_t parity, unsigned
     const bool all = named_and(1, kStEpi, ok);
     if (!all && threadIdx.x == 0) atomicCAS(&g_tc_fault, 0u, code);
     return all;
-}
-
-// x of one chunk for builder thread r: vectors idx = r + kStEpi k (8 channels
-// each); tokens from t_end on and channels from pw on read as zero.
-__device__ __forceinline__ void st_load_x(const ScanParams& p, int64_t xb, int t0, int t_end, int pw, int r,
-                                          uint4 (&v)[kStVec]) {
-    const __nv_bfloat16* xg = static_cast<const __nv_bfloat16*>(p.x);
-#pragma unroll
-    for (int k = 0; k < kStVec; ++k) {
-        const int idx = r + kStEpi * k, j = idx >> 3, c = idx & 7;
-        const int t = t0 + j;
-        v[k] = make_uint4(0u, 0u, 0u, 0u);
-        if (t < t_end) {
-            const __nv_bfloat16* src = xg + xb + (int64_t)t * p.s_x0 + 8 * c;
-            if (8 * c + 8 <= pw) {
-                v[k] = __ldg(reinterpret_cast<const uint4*>(src));
-            } else if (8 * c < pw) {
-                uint16_t e[8];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) e[q] = 8 * c + q < pw ? __bfloat16_as_ushort(src[q]) : (uint16_t)0;
-                v[k] = make_uint4(e[0] | (uint32_t)e[1] << 16, e[2] | (uint32_t)e[3] << 16, e[4] | (uint32_t)e[5] << 16,
-                                  e[6] | (uint32_t)e[7] << 16);
-            }
-        }
-    }
 }
 
 __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_constant__ TcMaps maps, ScanParams p,
@@ -1348,19 +1342,24 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
     const int t_begin = tl.run * p.run_tok;
     const int t_end = min(p.L, t_begin + p.run_tok);
     const int n_ch = (t_end - t_begin + kCS - 1) / kCS;
+    const int n_st = 2 * n_ch;  // steps; a step past t_end reads zeros
     const int64_t db = (int64_t)tl.seq * p.seq_dt + (int64_t)tl.h * p.s_dt1;
-    auto stage = [&](int q) { return sm + (uint32_t)(q % kStStages) * SO_STAGE; };
-    uint8_t* sXH = sm + SO_XW;
-    uint8_t* sXL = sXH + 16384;
-    auto t0_of = [&](int q) { return t_begin + (n_ch - 1 - q) * kCS; };  // visit order q -> chunk
+    auto t0_of = [&](int q) { return t_begin + (n_ch - 1 - q) * kCS; };       // visit order q -> chunk
+    auto ts_of = [&](int s) { return t0_of(s >> 1) + (s & 1) * kStHalf; };    // step s -> first token
+    auto sB = [&](int s) { return sm + SO_B + (uint32_t)(s % kStStages) * 16384u; };
+    auto sX = [&](int s) { return sm + SO_X + (uint32_t)(s % kStStages) * 8192u; };
+    auto sXW = [&](int s) { return sm + SO_XW + (uint32_t)(s & 1) * 16384u; };
 
     if (tid == 0) {
         for (int k = 0; k < kStStages; ++k) {
-            mbar_init(&bars.full[k], 1);
+            mbar_init(&bars.b_full[k], 1);
             mbar_init(&bars.b_done[k], 1);
+            mbar_init(&bars.x_full[k], 1);
         }
-        mbar_init(&bars.xw_full, kStEpi / 32);
-        mbar_init(&bars.xw_empty, 1);
+        for (int k = 0; k < 2; ++k) {
+            mbar_init(&bars.xw_full[k], kStEpi / 32);
+            mbar_init(&bars.xw_empty[k], 1);
+        }
         for (int k = 0; k < kStRing; ++k) {
             mbar_init(&bars.w_full[k], 1);
             mbar_init(&bars.w_empty[k], kStEpi / 32);
@@ -1375,47 +1374,58 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
     tc_fence_after();
     const uint32_t tm = tmem_base;
 
-    auto load = [&](int q) {
-        uint8_t* st = stage(q);
-        uint64_t* bar = &bars.full[q % kStStages];
-        const int t0 = t0_of(q);
-        mbar_expect_tx(bar, 2 * 16384);
-        tma_load_4d(st, &maps.b, bar, 0, g, t0, tl.seq);
-        tma_load_4d(st + 16384, &maps.b, bar, 64, g, t0, tl.seq);
+    auto load_b = [&](int s) {
+        uint64_t* bar = &bars.b_full[s % kStStages];
+        mbar_expect_tx(bar, 2 * 8192);
+        tma_load_4d(sB(s), &maps.b, bar, 0, g, ts_of(s), tl.seq);
+        tma_load_4d(sB(s) + 8192, &maps.b, bar, 64, g, ts_of(s), tl.seq);
+    };
+    auto load_x = [&](int s) {
+        uint64_t* bar = &bars.x_full[s % kStStages];
+        mbar_expect_tx(bar, 8192);
+        tma_load_4d(sX(s), &maps.x, bar, p0, tl.h, ts_of(s), tl.seq);
     };
 
     bool ok = true;
     if (is_mma) {
         if ((tid & 31) == 0) {
             prefetch_tmap(&maps.b);
-            for (int q = 0; q < kStStages && q < n_ch; ++q) load(q);
+            prefetch_tmap(&maps.x);
+            for (int s = 0; s < kStStages && s < n_st; ++s) {
+                load_b(s);
+                load_x(s);
+            }
             HX_PHASE_T(16, 256);
-            for (int q = 0; q < n_ch && ok; ++q) {
-                const int s = q % kStStages;
-                const uint32_t pf = (uint32_t)((q / kStStages) & 1);
-                if (!(ok = mbar_wait(&bars.full[s], pf, kWaitBudget))) break;
+            for (int s = 0; s < n_st && ok; ++s) {
+                const int st = s % kStStages;
+                const uint32_t pf = (uint32_t)((s / kStStages) & 1);
+                if (!(ok = mbar_wait(&bars.b_full[st], pf, kWaitBudget))) break;
                 HX_PHASE_T(17, 256);
-                if (!(ok = mbar_wait(&bars.xw_full, (uint32_t)(q & 1), kWaitBudget))) break;
+                if (!(ok = mbar_wait(&bars.xw_full[s & 1], (uint32_t)((s >> 1) & 1), kWaitBudget))) break;
                 HX_PHASE_T(18, 256);
                 tc_fence_after();
-                // one N = 128 MMA per K step: [xw_hi | xw_lo] side by side (16 KB apart)
-                const uint32_t aB = smem_u32(stage(q)), aXW = smem_u32(sXH);
+                // A = B rows of the step (M = 128 states in two 64-state atoms),
+                // B = [xw_hi | xw_lo] (N = 128 in two atoms), K = 64 tokens
+                const uint64_t dA = sdesc_sw128(smem_u32(sB(s)), 8192, 1024);
+                const uint64_t dX = sdesc_sw128(smem_u32(sXW(s)), 8192, 1024);
 #pragma unroll
-                for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16(tm, desc_mnmajor(aB, ks), desc_mnmajor(aXW, ks), ID_G4W, (q > 0 || ks > 0) ? 1u : 0u);
-                mma_commit(&bars.xw_empty);
-                mma_commit(&bars.b_done[s]);
+                for (int ks = 0; ks < 4; ++ks)
+                    mma_bf16(tm, desc_add(dA, 2048u * ks), desc_add(dX, 2048u * ks), ID_G4W, (s > 0 || ks > 0) ? 1u : 0u);
+                mma_commit(&bars.xw_empty[s & 1]);
+                mma_commit(&bars.b_done[st]);
                 HX_PHASE_T(19, 256);
-                if (q + kStStages < n_ch) {
-                    // B is free once these MMAs retire
-                    if (!(ok = mbar_wait(&bars.b_done[s], pf, kWaitBudget))) break;
-                    load(q + kStStages);
+                if (s + kStStages < n_st) {
+                    // the builders consumed x(s) before xw_full; B(s) is free once
+                    // these MMAs retire
+                    load_x(s + kStStages);
+                    if (!(ok = mbar_wait(&bars.b_done[st], pf, kWaitBudget))) break;
+                    load_b(s + kStStages);
                 }
                 HX_PHASE_T(20, 256);
             }
             if (!ok) {
                 atomicCAS(&g_tc_fault, 0u, kFaultMmaState);
-                mbar_wait(&bars.xw_empty, 0, kWaitBudget);
+                mbar_wait(&bars.xw_empty[0], 0, kWaitBudget);
             }
         }
         __syncwarp();
@@ -1449,28 +1459,30 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
         if ((tid & 31) == 0) lam_total = later / kLog2e;
         __syncwarp();
     } else {
-        // ---- xw builders ----------------------------------------------------
+        // ---- xw builders: two 16-byte x vectors per thread per step -------
         HX_PHASE(21);
-        const int64_t xb = (int64_t)tl.seq * p.seq_x + (int64_t)tl.h * p.s_x1 + p0;
-        uint4 cur[kStVec], nxt[kStVec];
-        if (n_ch > 0) st_load_x(p, xb, t0_of(0), t_end, pw, tid, cur);
-        for (int q = 0; q < n_ch; ++q) {
-            if (q + 1 < n_ch) st_load_x(p, xb, t0_of(q + 1), t_end, pw, tid, nxt);
-            const int slot = q % kStRing;
-            if (!(ok = st_wait(&bars.w_full[slot], (uint32_t)((q / kStRing) & 1), kFaultMmaState))) break;
+        for (int s = 0; s < n_st; ++s) {
+            const int q = s >> 1, slot = q % kStRing;
+            if ((s & 1) == 0) {
+                if (!(ok = st_wait(&bars.w_full[slot], (uint32_t)((q / kStRing) & 1), kFaultMmaState))) break;
+            }
             HX_PHASE(22);
-            if (q >= 1) {  // the single xw buffer: G4(q-1) retired
-                if (!(ok = st_wait(&bars.xw_empty, (uint32_t)((q - 1) & 1), kFaultMmaState))) break;
+            if (!(ok = st_wait(&bars.x_full[s % kStStages], (uint32_t)((s / kStStages) & 1), kFaultTmaState))) break;
+            if (s >= 2) {  // xw buffer s & 1 was last read by step s - 2
+                if (!(ok = st_wait(&bars.xw_empty[s & 1], (uint32_t)(((s - 2) >> 1) & 1), kFaultMmaState))) break;
             }
             HX_PHASE(23);
-            const float* wv = wring + slot * 128;
+            const float* wv = wring + slot * 128 + (s & 1) * kStHalf;
+            const uint8_t* x = sX(s);
+            uint8_t* xh = sXW(s);
 #pragma unroll
-            for (int k = 0; k < kStVec; ++k) {
+            for (int k = 0; k < 2; ++k) {
                 const int i = tid + kStEpi * k;
                 const int j = i >> 3, c = i & 7;
                 const uint32_t off = sw128_off(j, c);
                 const float wj = wv[j];
-                const uint32_t in[4] = {cur[k].x, cur[k].y, cur[k].z, cur[k].w};
+                const uint4 xr = *reinterpret_cast<const uint4*>(x + off);
+                const uint32_t in[4] = {xr.x, xr.y, xr.z, xr.w};
                 uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -1483,21 +1495,20 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
                     unpack_bf16x2(hi[e], ah, bh);
                     lo[e] = pack_bf16x2(a - ah, b - bh);
                 }
-                *reinterpret_cast<uint4*>(sXH + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(sXL + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<uint4*>(xh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4*>(xh + 8192 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
             fence_async_smem();
             __syncwarp();
             if ((tid & 31) == 0) {
-                mbar_arrive(&bars.xw_full);
-                mbar_arrive(&bars.w_empty[slot]);
+                mbar_arrive(&bars.xw_full[s & 1]);
+                if (s & 1) mbar_arrive(&bars.w_empty[slot]);
             }
-#pragma unroll
-            for (int k = 0; k < kStVec; ++k) cur[k] = nxt[k];
             HX_PHASE(25);
         }
-        // all G4 MMAs retired: the last chunk's commit
-        if (ok && n_ch > 0) ok = st_wait(&bars.xw_empty, (uint32_t)((n_ch - 1) & 1), kFaultMmaState);
+        // all G4 MMAs retired: the last step's commit
+        if (ok && n_st > 0)
+            ok = st_wait(&bars.xw_empty[(n_st - 1) & 1], (uint32_t)(((n_st - 1) >> 1) & 1), kFaultMmaState);
         tc_fence_after();
         if (ok) {
             const int64_t unit = ((int64_t)tl.seq * p.H + tl.h) * p.n_runs + tl.run;
@@ -1535,13 +1546,13 @@ using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, voi
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// 4-D bf16 map (inner, d1, tok, seq) with a 64 x 1 x 128 x 1 box, 128-byte
-// swizzle.  Coordinates past the extents read as zero.
+// 4-D bf16 map (inner, d1, tok, seq) with a 64 x 1 x box_tok x 1 box,
+// 128-byte swizzle.  Coordinates past the extents read as zero.
 bool make_map(EncodeFn fn, CUtensorMap* m, const void* base, int64_t inner, int64_t d1, int64_t tok, int64_t seq,
-              int64_t s1, int64_t s_tok, int64_t s_seq) {
+              int64_t s1, int64_t s_tok, int64_t s_seq, int box_tok = kCS) {
     cuuint64_t dims[4] = {(cuuint64_t)inner, (cuuint64_t)d1, (cuuint64_t)tok, (cuuint64_t)seq};
     cuuint64_t strides[3] = {(cuuint64_t)(s1 * 2), (cuuint64_t)(s_tok * 2), (cuuint64_t)(s_seq * 2)};
-    cuuint32_t box[4] = {64, 1, (cuuint32_t)kCS, 1};
+    cuuint32_t box[4] = {64, 1, (cuuint32_t)box_tok, 1};
     cuuint32_t es[4] = {1, 1, 1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1562,6 +1573,14 @@ bool make_ymap(EncodeFn fn, CUtensorMap* m, void* base, const ScanParams& p) {
 
 // TMA stores of y need unit channel stride, 16-byte multiples for the other
 // strides and a 16-byte aligned base.
+// Maps of the state kernel: x and B in 64-token boxes (its step).
+bool make_state_maps(EncodeFn fn, TcMaps* m, const ScanParams& p) {
+    const int64_t S = p.S;
+    std::memset(&m->c, 0, sizeof(m->c));
+    return make_map(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf) &&
+           make_map(fn, &m->b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf);
+}
+
 bool y_tma_ok(const ScanParams& p) {
     if (p.s_y2 != 1) return false;
     const int64_t st[3] = {p.s_y1, p.s_y0, p.seq_y};
@@ -1608,7 +1627,9 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* s
     const int64_t per_run = (int64_t)p.n_pslab * p.H * S;
     if (pl.need_state_kernel && do_a) {
         const int runs = pl.n_runs - 1;
-        tc_state_kernel<<<(unsigned)(per_run * runs), kStThreads, SMEM_STATE, st>>>(maps, p, runs);
+        TcMaps smaps;
+        if (!make_state_maps(fn, &smaps, p)) return cudaErrorInvalidValue;
+        tc_state_kernel<<<(unsigned)(per_run * runs), kStThreads, SMEM_STATE, st>>>(smaps, p, runs);
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
@@ -1632,10 +1653,7 @@ int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, 
     if (!fn) return cudaErrorNotSupported;
     TcMaps maps;
     const int64_t S = p.S;
-    if (!make_map(fn, &maps.x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x) ||
-        !make_map(fn, &maps.b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b) ||
-        !make_map(fn, &maps.c, p.C, p.N, p.G, p.L, S, p.s_c1, p.s_c0, p.seq_c))
-        return cudaErrorInvalidValue;
+    if (!make_state_maps(fn, &maps, p)) return cudaErrorInvalidValue;
     const int64_t per_run = (int64_t)p.n_pslab * p.H * S;
     tc_state_kernel<<<(unsigned)(per_run * pl.n_runs), kStThreads, SMEM_STATE, static_cast<cudaStream_t>(stream)>>>(
         maps, p, pl.n_runs);
