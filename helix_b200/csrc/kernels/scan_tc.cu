@@ -656,8 +656,9 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
 // whole accumulator slice at once.
 //
 //   warps 0-3    W_y   y = f_t D[i&1] -> smem (xw[i&1], free after G2) -> TMA store
-//   warps 4-7    W_m   D1[i&1] -> causal mask -> bf16 pairs into M (row per
-//                      thread, 64 columns per TMEM read)
+//   warps 4-7    W_m   D1[i&1] -> causal mask -> bf16 pairs written over
+//                      D1[i&1]'s first 64 columns (row per thread, 64 columns
+//                      per TMEM read)
 //   warps 8-11   W_c   S_{i+1} = D4 -> s1 (last chunk) / S~_{i+1} into D4 and,
 //                      as bf16, into smem for G3(i+1)
 //   warps 12-17  W_xw  x from global (one chunk prefetched in registers),
@@ -665,12 +666,14 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
 //   warp 18      TMA producer and MMA issuer (lane 0)
 //   warp 19      chunk vectors (w, f, exp(Lc_end)) into a 4-slot ring
 //
-// MMA issue order, chunk i:
-//   G1 C.B^T -> D1[i&1];  G4 B^T.xw_hi, B^T.xw_lo -> D4 (accumulating onto S~_i);
-//   G3 C.S~ -> D[i&1];  G2 M.xw_hi -> D[i&1] (A from TMEM);  C/B(i+2) once G3 retires.
+// MMA issue order, chunk i (G1 runs a chunk ahead):
+//   G4 B^T.xw_hi, B^T.xw_lo -> D4 (accumulating onto S~_i);  G3 C.S~ -> D[i&1];
+//   G1(i+1) C.B^T -> D1[(i+1)&1];  G2 mask(i).xw_hi -> D[i&1] (A from TMEM);
+//   C/B(i+2) once G3(i) retires.
 //
-// TMEM columns: D1 0-127 | D1' 128-255 | D4 256-319 | D 320-383 | D' 384-447 |
-//               M 448-511.
+// TMEM columns: D1 0-127 | D1' 128-255 (each holding its chunk's mask, packed
+//               in place, once W_m has read it) | D4 256-319 | D 320-383 |
+//               D' 384-447.
 // smem: C/B 2 x 64 KB | xw 2 x 32 KB | S~ bf16 16 KB | vector ring.
 // ---------------------------------------------------------------------------
 constexpr uint32_t OF_XW = 131072;
@@ -679,7 +682,7 @@ constexpr uint32_t OF_V = 212992;
 constexpr int kFRing = 4;
 constexpr int kFVec = 2 * 128 + 8;  // w | f | exp(Lc_end)
 static_assert(OF_V + kFRing * kFVec * 4 + 1024 <= SMEM_OUT, "fast path fits the general path's allocation");
-constexpr uint32_t TF_D4 = 256, TF_D = 320, TF_M = 448;
+constexpr uint32_t TF_D4 = 256, TF_D = 320;
 constexpr uint32_t ID_G4N = idesc_bf16(128, 64, true, true);
 constexpr float kFastSpan2 = 86.0f;  // ~59.6 nats
 // Warp w runs on SM sub-partition w % 4.  The MMA warp's sub-partition hosts
@@ -797,26 +800,36 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
         // ================= TMA producer + MMA issuer ========================
         if (lane == 0) {
             const uint32_t aS = smem_u32(sS);
+            const uint64_t dSm = sdesc_sw128(aS, 16384, 1024);
+            // G1 of chunk k -> D1[k & 1].  D1[k & 1] holds the mask of chunk
+            // k-2 (W_m packs it in place), read by G2(k-2): wait for that first.
+            auto issue_g1 = [&](int k) -> bool {
+                if (!mbar_wait(&cb_bar[k & 1], bpar(k), kWaitBudget)) return false;
+                if (k >= 2 && !mbar_wait(&bars.g2[k & 1], bpar(k - 2), kWaitBudget)) return false;
+                HX_TL(0, k);
+                tc_fence_after();
+                const uint32_t aC = smem_u32(sCB(k)), aB = aC + 32768;
+                const uint64_t dCk = sdesc_sw128(aC, 16, 1024), dBk = sdesc_sw128(aB, 16, 1024);
+                const uint32_t tD1 = tm + 128u * (uint32_t)(k & 1);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                    mma_bf16(tD1, desc_add(dCk, kmajor_off(ks)), desc_add(dBk, kmajor_off(ks)), ID_G1, ks > 0);
+                mma_commit(&bars.acc1[k & 1]);
+                HX_TL(1, k);
+                return true;
+            };
             HX_PHASE_T(1, kMmaTid);
+            if (n_ch > 0) ok = issue_g1(0);
+            // Issue order for chunk i: G4(i), G3(i), G1(i+1), G2(i).  G1 runs a
+            // chunk ahead so the tensor pipe has queued work while G2(i) waits
+            // for the mask of chunk i, and W_m gets a chunk of slack.
             for (int i = 0; i < n_ch && ok; ++i) {
                 const int b = i & 1;
                 const uint32_t par = (uint32_t)(i & 1);
                 const uint32_t aC = smem_u32(sCB(i)), aB = aC + 32768, aX = smem_u32(sXW(i));
-                const uint32_t tD1 = tm + 128u * (uint32_t)b, tD = tm + TF_D + 64u * (uint32_t)b;
-                // base descriptors; each K step below adds a constant
-                const uint64_t dCk = sdesc_sw128(aC, 16, 1024), dBk = sdesc_sw128(aB, 16, 1024);
+                const uint32_t tD = tm + TF_D + 64u * (uint32_t)b;
+                const uint64_t dCk = sdesc_sw128(aC, 16, 1024);
                 const uint64_t dBm = sdesc_sw128(aB, 16384, 1024), dXm = sdesc_sw128(aX, 16384, 1024);
-                const uint64_t dSm = sdesc_sw128(aS, 16384, 1024);
-                // D1[b]: W_m(i-2) read it before m_ready(i-2), which G2(i-2) waited for
-                if (!(ok = mbar_wait(&cb_bar[b], bpar(i), kWaitBudget))) break;
-                HX_TL(0, i);
-                HX_PHASE_T(2, kMmaTid);
-                tc_fence_after();
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16(tD1, desc_add(dCk, kmajor_off(ks)), desc_add(dBk, kmajor_off(ks)), ID_G1, ks > 0);
-                mma_commit(&bars.acc1[b]);
-                HX_TL(1, i);
                 // G4 accumulates onto S~_i, which W_c left in D4
                 if (!(ok = mbar_wait(&bars.xw_ready[b], bpar(i), kWaitBudget))) break;
                 if (!(ok = mbar_wait(&bars.d4_ready, par, kWaitBudget))) break;
@@ -843,16 +856,17 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
                     mma_bf16(tD, desc_add(dCk, kmajor_off(ks)), desc_add(dSm, 2048u * ks), ID_G3, ks > 0);
                 mma_commit(&bars.g3);
                 HX_TL(5, i);
+                if (i + 1 < n_ch && !(ok = issue_g1(i + 1))) break;
                 if (!(ok = mbar_wait(&bars.m_ready, par, kWaitBudget))) break;
                 HX_TL(6, i);
                 HX_PHASE_T(5, kMmaTid);
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16_ts(tD, tm + TF_M + 8u * (uint32_t)ks, desc_add(dXm, 2048u * ks), ID_G2, 1u);
+                    mma_bf16_ts(tD, tm + 128u * (uint32_t)b + 8u * (uint32_t)ks, desc_add(dXm, 2048u * ks), ID_G2, 1u);
                 mma_commit(&bars.g2[b]);
                 HX_TL(7, i);
-                // G1, G4, G3 of chunk i were the last readers of C/B[b]
+                // G1(i), G4(i) and G3(i) were the last readers of C/B[b]
                 if (!(ok = mbar_wait(&bars.g3, par, kWaitBudget))) break;
                 if (i + 2 < n_ch) load_cb_chunk(maps, sCB(i + 2), &cb_bar[b], ot.g, t_begin + (i + 2) * kCS, tl.seq);
                 HX_TL(8, i);
@@ -1034,11 +1048,13 @@ __device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& 
             if (leader) HX_TL(9, i);
             HX_PHASE_T(11, 32 * kWarpM);
             tc_fence_after();
+            // The mask goes in place: packed pairs over D1[i&1]'s first 64
+            // columns.  Each thread owns its row, and the columns a pass writes
+            // (32 half .. +31) were read in this or the previous pass.  Columns
+            // are read 64 at a time, and only where some row of this lane
+            // quarter needs them.
             const uint32_t src = tm + lane_off + 128u * (uint32_t)(i & 1);
-            const uint32_t dst = tm + lane_off + TF_M;
-            // M was last read by G2(i-1), which retired before G1(i) (acc1 above).
-            // Columns are read 64 at a time, and only where some row of this
-            // lane quarter needs them.
+            const uint32_t dst = src;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 if (64 * half <= rmax) {
