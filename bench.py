@@ -215,7 +215,12 @@ def bench_lsplit(a, rank: int, world: int, local: int) -> int:
     d_scan = helix_b200.desc_from_tensors(t["x"], t["dt"], t["B"], t["s0"], None, multipass=True,
                                           compute=a.compute)
     ctx = helix_b200._ctx_for(t["x"], None)
-    launches = 3 + ((3 if a.compute == "bf16" else 2) if ctx.scratch_size(d_scan) else 1)
+    n_sb = ctx.scratch_size(d_scan)
+    has_runs = n_sb >= t["x"].shape[0] * t["x"].shape[2] * t["x"].shape[3] * t["s0"].shape[-1] * 4
+    if a.compute == "bf16":
+        launches = 3 + (2 if has_runs else 0) + 2
+    else:
+        launches = 3 + (2 if n_sb else 1)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -373,9 +378,14 @@ def main():
         ms = timed(step, a.steps)
     total_ms = max_over_ranks(sum(ms))
     ms_per_step = total_ms / a.steps
-    # state + carry + output kernels with runs (tcgen05 family), state + output
-    # (fp32 family), or the output kernel alone (single run)
-    launches = (3 if a.compute == "bf16" else 2) if nbytes > 0 else 1
+    # tcgen05 family: state + carry kernels when the scratch holds run states,
+    # then the output kernels (fast path, general path); fp32 family: state +
+    # output kernels with runs, the output kernel alone with one
+    has_runs = nbytes >= x.shape[0] * x.shape[2] * x.shape[3] * s0.shape[-1] * 4
+    if a.compute == "bf16":
+        launches = (2 if has_runs else 0) + 2
+    else:
+        launches = 2 if nbytes > 0 else 1
 
     # ---- per-kernel attribution (same steps, passes split) --------------
     def only(p):
@@ -387,8 +397,8 @@ def main():
                 os.environ.pop("HELIX_ONLY_PASS", None)
         return f
     ms_c = max_over_ranks(sum(timed(only("C"), a.steps))) / a.steps
-    ms_a = max_over_ranks(sum(timed(only("A"), a.steps))) / a.steps if launches > 1 else 0.0
-    ms_b = max_over_ranks(sum(timed(only("B"), a.steps))) / a.steps if launches > 2 else 0.0
+    ms_a = max_over_ranks(sum(timed(only("A"), a.steps))) / a.steps if (has_runs or a.compute != "bf16" and nbytes > 0) else 0.0
+    ms_b = max_over_ranks(sum(timed(only("B"), a.steps))) / a.steps if has_runs and a.compute == "bf16" else 0.0
 
     hbm, tc, peak_kind = peaks()
     e_io = 2 if shape.io == "bf16" else 4

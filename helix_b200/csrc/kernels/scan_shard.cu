@@ -25,10 +25,10 @@ __global__ void __launch_bounds__(kThreads) shard_fold_kernel(ScanParams p, floa
     const int64_t e = gid - head_lin * per_head;
     const int seq = (int)(head_lin / p.H), h = (int)(head_lin % p.H);
     const int c = (int)(e / p.N), n = (int)(e % p.N);
-    const int64_t unit0 = head_lin * p.n_runs;
+    const int64_t unit0 = head_lin * p.run_slots;
     float S = 0.0f, total = 0.0f;
     int r = 0;
-    for (; r + 4 <= p.n_runs; r += 4) {
+    for (; r + 4 <= p.state_runs; r += 4) {
         float a[4], v[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -41,7 +41,7 @@ __global__ void __launch_bounds__(kThreads) shard_fold_kernel(ScanParams p, floa
             total += a[k];
         }
     }
-    for (; r < p.n_runs; ++r) {
+    for (; r < p.state_runs; ++r) {
         const float a = p.lam[unit0 + r];
         S = fmaf(expf(a), S, p.agg[(unit0 + r) * per_head + e]);
         total += a;

@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1) simt_state_kernel(ScanParams p, i
         __syncthreads();
     }
 
-    const int64_t unit = ((int64_t)tl.seq * p.H + tl.h) * p.n_runs + tl.run;
+    const int64_t unit = ((int64_t)tl.seq * p.H + tl.h) * p.run_slots + tl.run;
     if (tl.slab == 0 && tid == 0) p.lam[unit] = later;
 
     // Transpose through smem so the (chan, state) rows go out coalesced.
@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) simt_out_kernel(ScanParams p) {
         // The carry loop below maps threads to (c, n) differently when
         // N < NMAX, so the fill must be complete first.
         __syncthreads();
-        const int64_t unit0 = ((int64_t)tl.seq * p.H + tl.h) * p.n_runs;
+        const int64_t unit0 = ((int64_t)tl.seq * p.H + tl.h) * p.run_slots;
         for (int r = 0; r < tl.run; ++r) {
             const float a = expf(p.lam[unit0 + r]);
             const float* ag = p.agg + (unit0 + r) * (int64_t)p.P * N + (int64_t)p0 * N;
@@ -389,7 +389,7 @@ int launch_simt_t(const Plan& pl, const ScanParams& p, int n_seq, cudaStream_t s
     const bool do_c = !only || *only == 'C';
     const int64_t per_run = (int64_t)p.n_pslab * p.H;
     if (pl.need_state_kernel && do_a) {
-        const int runs = pl.n_runs - 1;
+        const int runs = pl.state_runs;
         simt_state_kernel<CS, NMAX, BF16>
             <<<(unsigned)(per_run * runs * n_seq), kThreads, SM::state_bytes, st>>>(p, runs);
         const cudaError_t e = cudaGetLastError();
@@ -410,7 +410,7 @@ int launch_simt_states_t(const Plan& pl, const ScanParams& p, cudaStream_t st) {
     using SM = SimtSmem<CS, NMAX>;
     const int64_t per_run = (int64_t)p.n_pslab * p.H;
     simt_state_kernel<CS, NMAX, BF16>
-        <<<(unsigned)(per_run * pl.n_runs * p.S), kThreads, SM::state_bytes, st>>>(p, pl.n_runs);
+        <<<(unsigned)(per_run * pl.state_runs * p.S), kThreads, SM::state_bytes, st>>>(p, pl.state_runs);
     return cudaGetLastError();
 }
 

@@ -4,22 +4,19 @@
 // which narrows only the GEMM operands and keeps the carry fp32).
 //
 // Same run decomposition as the fp32 family (runtime/internal.h).  Chunks are
-// 128 tokens so every GEMM has M = 128 (one TMEM lane per row):
+// 128 tokens so every GEMM has M = 128 (one TMEM lane per row).  Kernels:
 //
-//   G1  D1[t][j] = C[t][:] . B[j][:]            A = C  (K-major, TMA)   B = B  (K-major, TMA)
-//   G3  D3[t][p] = C[t][:] . S[:][p]            A = C                   B = S  (MN-major, threads)
-//   G4  D4[n][p] = sum_j B[j][n] xw[j][p]       A = B  (MN-major, TMA)  B = xw (MN-major, threads)
-//       xw = dt_j exp(Lc_end - Lc_j) x[j][p], split into bf16 hi + lo so the
-//       state update keeps ~16 mantissa bits (two MMAs into D4)
-//   M'[t][j] = D1[t][j] exp(Lc_t - Lc_j) dt_j for j <= t   (epilogue, bf16, K-major smem)
-//   G2  D2[t][p] = M'[t][:] . x[:][p]           A = M' (K-major)        B = x  (MN-major, TMA)
-//   y = D2 + exp(Lc_t) D3;   S <- exp(Lc_end) S + D4   (S kept fp32 in registers)
+//   tc_state_kernel        the state each run leaves from a zero start (G4 over
+//                          the run) and its log-decay
+//   tc_carry_kernel        run states -> the states entering each output span
+//   tc_out_kernel          the output pass, fast path: two 64-channel slabs of
+//                          one group per CTA, transposed GEMMs (see below)
+//   tc_out_general_kernel  the output pass for the tiles the fast path leaves
+//                          (chunks that decay too far for its scaling): one
+//                          slab at a time, decay folded into the mask
 //
-// Threads: 256 = two warpgroups; warp w reads TMEM lanes 32*(w%4).., and the
-// two warpgroups split the accumulator columns in halves.  Thread 0 issues
-// TMA and MMA.  Every mbarrier wait is bounded: on expiry the block agrees
-// (vote), records a fault code readable with helix_device_fault(), releases
-// its TMEM and returns.
+// Every mbarrier wait is bounded: on expiry the kernel records a fault code
+// readable with helix_device_fault(), releases its TMEM and returns.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -47,7 +44,7 @@ extern __device__ unsigned long long hx_phase_cycles[32];
 // Timeline of one CTA (blockIdx.x == HX_TL_CTA): clock64 of event `ev` in
 // chunk `i`.
 extern __device__ long long hx_tl[32 * 64];
-#define HX_TL_CTA 160
+#define HX_TL_CTA 40
 #define HX_TL(ev, i)                                                          \
     do {                                                                      \
         if (blockIdx.x == HX_TL_CTA && (i) < 64) hx_tl[(ev) * 64 + (i)] = clock64(); \
@@ -133,12 +130,15 @@ __device__ __forceinline__ void warp_chunk_prefix(const ScanParams& p, int64_t d
     *total = __shfl_sync(0xffffffffu, incl, 31);
 }
 
+// Raw dt of tokens t0 + 4 lane .. +3.  Tokens at or past t_end read token
+// t_end - 1 instead (every consumer masks them by the chunk length): the loads
+// carry no condition, so nothing waits for them before their first use.
 __device__ __forceinline__ void warp_load_dt(const ScanParams& p, int64_t db, int t0, int t_end, float (&raw)[4]) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const int t = t0 + 4 * lane + k;
-        raw[k] = t < t_end ? p.dt[db + (int64_t)t * p.s_dt0] : 0.0f;
+        const int t = min(t0 + 4 * lane + k, t_end - 1);
+        raw[k] = __ldg(p.dt + db + (int64_t)t * p.s_dt0);
     }
 }
 
@@ -207,27 +207,82 @@ __device__ __forceinline__ void warp_arrive(uint64_t* bar) {
     if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
-// One CTA's share of the output pass: (seq, head, 64-channel slab, run).
+// Output kernel tiles.  A CTA owns a "pair": two 64-channel slabs of one
+// group (two heads, or two slabs of one head when P > 64) over a span of
+// out_k consecutive runs.  With an odd slab count per group the last pair's
+// second slab is empty (valid = 0, pw = 0: reads zeros, writes nothing).
+// CTA order: pair fastest, then group, span and sequence, so the CTAs that
+// share a group's C and B run side by side.
+struct SlabRef {
+    int valid, h, slab, p0, pw;
+    float Ah;
+    int64_t db, unit0;
+};
+struct PairTile {
+    int seq, g, run0, last;
+    int t_begin, t_end, n_ch;
+    SlabRef s[2];
+};
+
+__device__ __forceinline__ PairTile pair_tile(const ScanParams& p, int b = (int)blockIdx.x) {
+    PairTile o;
+    const int q = b % p.n_pair;
+    b /= p.n_pair;
+    o.g = b % p.G;
+    b /= p.G;
+    const int span = b % p.n_out;
+    o.seq = b / p.n_out;
+    o.run0 = span * p.out_k;
+    o.last = span == p.n_out - 1;
+    o.t_begin = o.run0 * p.run_tok;
+    o.t_end = min(p.L, o.t_begin + p.out_k * p.run_tok);
+    o.n_ch = (o.t_end - o.t_begin + kCS - 1) / kCS;
+    const int units = p.hpg * p.n_pslab;
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+        SlabRef& r = o.s[v];
+        const int u = 2 * q + v;
+        r.valid = u < units;
+        const int uu = r.valid ? u : 2 * q;
+        r.h = o.g * p.hpg + uu / p.n_pslab;
+        r.slab = uu % p.n_pslab;
+        r.p0 = r.slab * kSlab;
+        r.pw = r.valid ? min(kSlab, p.P - r.p0) : 0;
+        r.Ah = p.A[(int64_t)r.h * p.s_a];
+        r.db = (int64_t)o.seq * p.seq_dt + (int64_t)r.h * p.s_dt1;
+        r.unit0 = ((int64_t)o.seq * p.H + r.h) * p.run_slots;
+    }
+    return o;
+}
+
+// One slab of a pair, for the general path (one slab at a time).
 struct OutTile {
     Tile tl;
     int p0, pw, g;
     float Ah;
     int t_begin, t_end, n_ch;
     int64_t db, unit0;
+    int run0, last;
 };
 
-__device__ __forceinline__ OutTile out_tile(const ScanParams& p) {
+__device__ __forceinline__ OutTile slab_tile(const PairTile& pt, int v) {
     OutTile o;
-    o.tl = decode_tile(blockIdx.x, p.n_pslab, p.H, p.n_runs);
-    o.p0 = o.tl.slab * kSlab;
-    o.pw = min(kSlab, p.P - o.p0);
-    o.g = o.tl.h / p.hpg;
-    o.Ah = p.A[(int64_t)o.tl.h * p.s_a];
-    o.t_begin = o.tl.run * p.run_tok;
-    o.t_end = min(p.L, o.t_begin + p.run_tok);
-    o.n_ch = (o.t_end - o.t_begin + kCS - 1) / kCS;
-    o.db = (int64_t)o.tl.seq * p.seq_dt + (int64_t)o.tl.h * p.s_dt1;
-    o.unit0 = ((int64_t)o.tl.seq * p.H + o.tl.h) * p.n_runs;
+    const SlabRef& r = pt.s[v];
+    o.tl.seq = pt.seq;
+    o.tl.run = pt.run0;
+    o.tl.h = r.h;
+    o.tl.slab = r.slab;
+    o.p0 = r.p0;
+    o.pw = r.pw;
+    o.g = pt.g;
+    o.Ah = r.Ah;
+    o.t_begin = pt.t_begin;
+    o.t_end = pt.t_end;
+    o.n_ch = pt.n_ch;
+    o.db = r.db;
+    o.unit0 = r.unit0;
+    o.run0 = pt.run0;
+    o.last = pt.last;
     return o;
 }
 
@@ -241,10 +296,13 @@ __device__ __forceinline__ void load_cb_chunk(const TcMaps& maps, uint8_t* st, u
     tma_load_4d(st + 49152, &maps.b, bar, 64, g, t0, seq);
 }
 
+// set: 0 for the first slab a CTA runs here, 1 for the second; each has its
+// own barriers (and its own C/B barriers, cb_bar), so nothing is reused.
 __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams& p, const OutTile& ot, uint8_t* sm,
-                                            uint32_t tm, uint64_t* cb_bar) {
+                                            uint32_t tm, uint64_t* cb_bar, int set) {
     float* ring = reinterpret_cast<float*>(sm + OO_V);
-    __shared__ OutBars bars;
+    __shared__ OutBars bars_all[2];
+    OutBars& bars = bars_all[set];
 
     HX_PHASE_START;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -518,12 +576,12 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
         {
             const float* src;
             int64_t sc;
-            if (tl.run == 0) {
+            if (ot.run0 == 0) {
                 const int sq = p.has_ids ? p.ids[tl.seq] : tl.seq;
                 src = p.s0 + (int64_t)sq * p.seq_s + (int64_t)tl.h * p.s_s0 + (int64_t)p0 * p.s_s1 + row;
                 sc = p.s_s1;
             } else {
-                src = p.agg + (unit0 + tl.run - 1) * (int64_t)p.P * p.N + (int64_t)p0 * p.N + row;
+                src = p.agg + (unit0 + ot.run0 - 1) * (int64_t)p.P * p.N + (int64_t)p0 * p.N + row;
                 sc = p.N;
             }
 #pragma unroll 1
@@ -577,7 +635,7 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
             warp_arrive(&bars.s_ready);
             HX_PHASE_T(27, 384);
         }
-        if (ok && tl.run == p.n_runs - 1) {
+        if (ok && ot.last) {
             float* s1 = p.s1 + (int64_t)tl.seq * p.seq_s + (int64_t)tl.h * p.s_s0 + (int64_t)p0 * p.s_s1 + row;
             tc_fence_after();
 #pragma unroll 1
@@ -638,525 +696,622 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
 }
 
 // ---------------------------------------------------------------------------
-// Output kernel, fast path.  With f_t = exp(Lc_t - Lc_end) and the G4 operand
-// xw_j = dt_j exp(Lc_end - Lc_j) x_j, the chunk's output is
+// Output kernel, fast path: both slabs of a pair at once, transposed so the
+// slab channels are the MMA's M dimension (M = 128 = two 64-channel slabs).
+// With f_t = exp(Lc_t - Lc_end), xw_j = dt_j exp(Lc_end - Lc_j) x_j and
+// S~ = exp(Lc_end) S (S the state entering the chunk), per slab
 //
-//   y_t = f_t [ C_t . S~ + sum_{j<=t} (C_t . B_j) xw_j ],   S~ = exp(Lc_end) S
+//   y_t = f_t [ C_t . S~ + sum_{j<=t} (C_t . B_j) xw_j ]
+//   S_next = S~ + sum_j B_j (x) xw_j
 //
-// so G3 (C.S~) and G2 (masked D1 . xw_hi) share one accumulator, the masked
-// D1 needs no exponentials, and x is only read to build xw.  It is exact
-// algebra; the scaling factors stay inside fp32/bf16 range while no chunk of
-// the run decays by more than kFastSpan2 (log2 units), which the kernel
-// prologue checks (runs that fail take out_general).
+// which is exact algebra; the scaling factors stay inside fp32/bf16 range
+// while no chunk of the span decays by more than kFastSpan2 (log2 units),
+// which the kernel prologue checks for both slabs (tiles that fail go to
+// tc_out_general_kernel).  The chunk's MMAs, all N = 128:
 //
-// The carried state lives in the G4 accumulator itself: W_c writes S~_i
-// there and G4(i) accumulates B^T.xw_hi and B^T.xw_lo onto it, leaving
-// S_{i+1}.  One TMEM read per chunk per role: under concurrent MMA traffic a
-// TMEM load round trip costs hundreds of cycles, so every role reads its
-// whole accumulator slice at once.
+//   G1    D1[t][j]   = C . B^T              A = C (K-major)     B = B (K-major)
+//   G3^T  Y[c][t]    = S~^T . C^T           A = S~^T (TMEM, bf16)  B = C (K-major)
+//   G4^T  D4[c][n]  += xw^T . B  (hi, lo)   A = xw (MN-major)   B = B (MN-major)
+//   G2^T  Y[c][t]   += xw_hi^T . mask^T     A = xw (MN-major)   B = mask (K-major)
 //
-//   warps 0-3    W_y   y = f_t D[i&1] -> smem (xw[i&1], free after G2) -> TMA store
-//   warps 4-7    W_m   D1[i&1] -> causal mask -> bf16 pairs written over
-//                      D1[i&1]'s first 64 columns (row per thread, 64 columns
-//                      per TMEM read)
-//   warps 8-11   W_c   S_{i+1} = D4 -> s1 (last chunk) / S~_{i+1} into D4 and,
-//                      as bf16, into smem for G3(i+1)
-//   warps 12-17  W_xw  x from global (one chunk prefetched in registers),
-//                      xw = w x -> bf16 hi | lo, two buffers
-//   warp 18      TMA producer and MMA issuer (lane 0)
-//   warp 19      chunk vectors (w, f, exp(Lc_end)) into a 4-slot ring
+// with c the channel of either slab (TMEM lane), so y leaves TMEM with
+// consecutive lanes on consecutive channels: coalesced stores, no staging.
+// The causal mask (D1 with j > t zeroed, bf16) is written over the chunk's C
+// once G3 has read it; the carried state lives in the G4 accumulator D4 (the
+// epilogue scales it to S~ in place and leaves a bf16 copy as G3's operand).
 //
-// MMA issue order, chunk i (G1 runs a chunk ahead):
-//   G4 B^T.xw_hi, B^T.xw_lo -> D4 (accumulating onto S~_i);  G3 C.S~ -> D[i&1];
-//   G1(i+1) C.B^T -> D1[(i+1)&1];  G2 mask(i).xw_hi -> D[i&1] (A from TMEM);
-//   C/B(i+2) once G3(i) retires.
+// 16 warps (128 registers per thread):
+//   warps 0-7     epilogue, lane quarter w & 3, column half w >> 2, per chunk:
+//                 the mask of D1(i) -> smem over C(i) (after G3(i)); S_{i+1}
+//                 -> S~_{i+1} in D4 and its bf16 copy (after G4(i)); y(i) =
+//                 f_t Y -> global (after G2(i)), one 128-byte row per store;
+//                 s1 after the span's last chunk, through shared memory
+//   warps 8, 9, 11, 12, 13, 15   xw = w x as bf16 hi | lo (x one chunk
+//                 ahead in registers): lo once G4(i-1) retired, hi once
+//                 G2(i-1) retired
+//   warp 10       TMA producer and MMA issuer (lane 0)
+//   warp 14       chunk vectors of both slabs (w, f, exp(Lc_end)) into a ring
 //
-// TMEM columns: D1 0-127 | D1' 128-255 (each holding its chunk's mask, packed
-//               in place, once W_m has read it) | D4 256-319 | D 320-383 |
-//               D' 384-447.
-// smem: C/B 2 x 64 KB | xw 2 x 32 KB | S~ bf16 16 KB | vector ring.
+// MMA issue order per chunk: G3^T(i), G4^T(i), G2^T(i), G1(i+1); C/B(i+2)
+// into chunk i's stage once G2(i) retired.
+//
+// TMEM columns: D1 0-127 | Y 128-255 | D4 256-383 | S~ (bf16 pairs) 384-447.
+// smem: C/B 2 x 64 KB | xw hi 32 KB | xw lo 32 KB (slab tiles 16 KB apart) |
+//       vector ring | raw dt ring.  The span-entry state is staged over the
+//       xw buffers before the first chunk.
 // ---------------------------------------------------------------------------
-constexpr uint32_t OF_XW = 131072;
-constexpr uint32_t OF_S = 196608;
-constexpr uint32_t OF_V = 212992;
-constexpr int kFRing = 4;
-constexpr int kFVec = 2 * 128 + 8;  // w | f | exp(Lc_end)
-static_assert(OF_V + kFRing * kFVec * 4 + 1024 <= SMEM_OUT, "fast path fits the general path's allocation");
-constexpr uint32_t TF_D4 = 256, TF_D = 320;
-constexpr uint32_t ID_G4N = idesc_bf16(128, 64, true, true);
+constexpr uint32_t OP_XW = 131072;
+constexpr uint32_t OP_V = 196608;
+constexpr int kPRing = 4;
+constexpr int kPSlot = 264;              // per slab: w[128] | f[128] | exp(Lc_end) | pad
+constexpr int kPVec = 2 * kPSlot;
+constexpr uint32_t OP_DT = OP_V + kPRing * kPVec * 4;  // vector warp's raw dt ring, 4 x 2 x 128 floats
+static_assert(OP_DT + 4 * 256 * 4 + 1024 <= SMEM_OUT, "fast path fits the general path's allocation");
+constexpr uint32_t TP_D1 = 0, TP_Y = 128, TP_D4 = 256, TP_S = 384;
+constexpr uint32_t ID_P_KK = idesc_bf16(128, 128, false, false);  // G1, G3^T
+constexpr uint32_t ID_P_MM = idesc_bf16(128, 128, true, true);    // G4^T
+constexpr uint32_t ID_P_MK = idesc_bf16(128, 128, true, false);   // G2^T
 constexpr float kFastSpan2 = 86.0f;  // ~59.6 nats
-// Warp w runs on SM sub-partition w % 4.  The MMA warp's sub-partition hosts
-// only the light vector warp and one warp of each TMEM role: an ALU-heavy
-// neighbour (the xw builders) slows its MMA issue by about a third.
-constexpr int kWarpY = 0, kWarpM = 4, kWarpC = 8, kWarpXw = 12, kWarpMma = 14, kWarpVec = 18;
-constexpr int kXwWarps = 6;  // warps 12, 13, 15, 16, 17, 19
-__device__ __forceinline__ int xw_index(int warp) { return warp < 14 ? warp - 12 : warp < 18 ? warp - 13 : warp - 14; }
-constexpr int kXwThreads = 32 * kXwWarps;
-constexpr int kXwVec = (1024 + kXwThreads - 1) / kXwThreads;
-constexpr int kMmaTid = 32 * kWarpMma;
-static_assert(kOutThreads / 32 == 20, "warp map of the fast path assumes 20 warps");
+// 16 warps, four per SM sub-partition, so each thread may hold 128 registers
+// (a sub-partition's 16K registers are shared by its warps).
+constexpr int kPThreads = 512;
+constexpr int kPEpi = 8;             // warps 0-7
+constexpr int kPWarpMma = 10, kPWarpVec = 14;  // sub-partition 2, shared with no builder
+constexpr int kPBld = 6;             // builder warps: 8, 9, 11, 12, 13, 15
+constexpr int kPBldThreads = 32 * kPBld;
+constexpr int kPV = (2048 + kPBldThreads - 1) / kPBldThreads;  // 16-byte vectors per builder thread
+constexpr int kPMmaTid = 32 * kPWarpMma;
+__device__ __forceinline__ int bld_index(int warp) { return warp < 10 ? warp - 8 : warp < 14 ? warp - 9 : warp - 10; }
 
-struct FastBars {
-    uint64_t xw_ready[2], xw_free[2], acc1[2], g2[2], d_free[2], m_ready, g4, d4_ready, s_ready, g3;
-    uint64_t v_full[kFRing], v_empty[kFRing];
+struct PairBars {
+    uint64_t s_ready, y_free, m_ready, d1_free, xw_ready, s1_ready;
+    uint64_t g3, g4, g2, fin;
+    uint64_t v_full[kPRing], v_empty[kPRing];
 };
 
-// Bounded wait agreed by one role's warps on named barrier `id`.
-__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, int id, int nthreads, bool leader) {
-    const bool ok = mbar_wait(bar, parity, kWaitBudget);
-    const bool all = named_and(id, nthreads, ok);
-    if (!all && leader) atomicCAS(&g_tc_fault, 0u, kFaultMmaOut);
-    return all;
+// Bounded wait, agreed by the calling warp; records a fault when it expires.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, parity, kWaitBudget));
+    if (!ok && (threadIdx.x & 31) == 0) atomicCAS(&g_tc_fault, 0u, kFaultMmaOut);
+    return ok;
 }
 
-// x of chunk i for W_xw thread r (0..kXwThreads-1): up to kXwVec 16-byte
-// vectors of 8 channels (vector idx = r + kXwThreads k of the chunk's 1024);
-// tokens past the run and channels past P read as zero.
-__device__ __forceinline__ void load_x_chunk(const ScanParams& p, const OutTile& ot, int r, int i,
-                                             uint4 (&v)[kXwVec]) {
-    const int64_t xb = (int64_t)ot.tl.seq * p.seq_x + (int64_t)ot.tl.h * p.s_x1 + ot.p0;
+// x of chunk i for builder thread r: vector idx = r + kPBldThreads k of the
+// chunk's 2048 (token j = idx >> 4, slab (idx >> 3) & 1, channels 8 (idx & 7)
+// .. +7).  The fast path runs only when P is a multiple of 8, so every vector
+// lies inside or outside its slab as a whole.  Vectors are loaded without a
+// condition (ones that do not exist read token t_end - 1 or the tensor's
+// first vector, and x_valid() zeroes them where they are used), so nothing
+// waits for the loads before their use.
+__device__ __forceinline__ bool x_valid(const PairTile& pt, int idx, int i) {
+    const int j = idx >> 4, sl = (idx >> 3) & 1, c = idx & 7;
+    const int pw = sl ? pt.s[1].pw : pt.s[0].pw;
+    return idx < 2048 && pt.t_begin + i * kCS + j < pt.t_end && 8 * c < pw;
+}
+__device__ __forceinline__ void load_x_pair(const ScanParams& p, const PairTile& pt, int r, int i,
+                                            uint4 (&v)[kPV]) {
     const __nv_bfloat16* xg = static_cast<const __nv_bfloat16*>(p.x);
 #pragma unroll
-    for (int k = 0; k < kXwVec; ++k) {
-        const int idx = r + kXwThreads * k, j = idx >> 3, c = idx & 7;
-        const int t = ot.t_begin + i * kCS + j;
-        v[k] = make_uint4(0u, 0u, 0u, 0u);
-        if (idx < 1024 && t < ot.t_end) {
-            const __nv_bfloat16* src = xg + xb + (int64_t)t * p.s_x0 + 8 * c;
-            if (8 * c + 8 <= ot.pw) {
-                v[k] = __ldg(reinterpret_cast<const uint4*>(src));
-            } else if (8 * c < ot.pw) {
-                uint16_t e[8];
+    for (int k = 0; k < kPV; ++k) {
+        const int idx = r + kPBldThreads * k, j = idx >> 4, sl = (idx >> 3) & 1, c = idx & 7;
+        const int t = min(pt.t_begin + i * kCS + j, pt.t_end - 1);
+        const SlabRef sr = sl ? pt.s[1] : pt.s[0];
+        const bool in = idx < 2048 && 8 * c < sr.pw;
+        const __nv_bfloat16* src =
+            xg + (int64_t)pt.seq * p.seq_x + (int64_t)t * p.s_x0 + (int64_t)sr.h * p.s_x1 + sr.p0 + 8 * c;
+        v[k] = __ldg(reinterpret_cast<const uint4*>(in ? src : xg));
+    }
+}
+
+// State tile of a pair in shared memory: row r = 64 v + c (slab v, channel
+// c), state n at word 128 r + (n ^ (r & 31)).  The XOR keeps both access
+// patterns free of bank conflicts: a warp on 32 consecutive n of one row
+// (global side) and a warp on one n of 32 consecutive rows (TMEM lane side).
+__device__ __forceinline__ uint32_t st_word(int r, int n) { return (uint32_t)(128 * r + (n ^ (r & 31))); }
+
+// The span-entry states of both slabs -> st (fp32, st_word layout), by the
+// 256 epilogue threads (et = 0..255) with coalesced loads: s0[ids[seq]] for
+// the first span, the carry kernel's slot otherwise; zero past the slab.
+__device__ __forceinline__ void load_state_tile(const ScanParams& p, const PairTile& pt, float* st, int et) {
+    const int sq = p.has_ids ? p.ids[pt.seq] : pt.seq;
+    const float* src[2];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) e[q] = 8 * c + q < ot.pw ? __bfloat16_as_ushort(src[q]) : (uint16_t)0;
-                v[k] = make_uint4(e[0] | (uint32_t)e[1] << 16, e[2] | (uint32_t)e[3] << 16, e[4] | (uint32_t)e[5] << 16,
-                                  e[6] | (uint32_t)e[7] << 16);
+    for (int v = 0; v < 2; ++v) {
+        const SlabRef& sr = pt.s[v];
+        src[v] = pt.run0 == 0 ? p.s0 + (int64_t)sq * p.seq_s + (int64_t)sr.h * p.s_s0 + (int64_t)sr.p0 * p.s_s1
+                              : p.agg + (sr.unit0 + pt.run0 - 1) * (int64_t)p.P * p.N + (int64_t)sr.p0 * p.N;
+    }
+    const int64_t rs = pt.run0 == 0 ? p.s_s1 : p.N;  // row (channel) stride
+    const bool vec = (rs & 3) == 0 && ((reinterpret_cast<uintptr_t>(src[0]) | reinterpret_cast<uintptr_t>(src[1])) & 15) == 0;
+    if (vec) {  // 16 float4 per thread (a warp on one 512-byte row), one slab at a time
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float4 f[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const int i4 = et + 256 * (8 * h + m), r = i4 >> 5, n = 4 * (i4 & 31), c = r & 63;
+                const int pw = h ? pt.s[1].pw : pt.s[0].pw;
+                f[m] = c < pw ? __ldg(reinterpret_cast<const float4*>(src[h] + (int64_t)c * rs + n))
+                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const int i4 = et + 256 * (8 * h + m), r = i4 >> 5, n = 4 * (i4 & 31);
+                st[st_word(r, n)] = f[m].x;
+                st[st_word(r, n + 1)] = f[m].y;
+                st[st_word(r, n + 2)] = f[m].z;
+                st[st_word(r, n + 3)] = f[m].w;
+            }
+        }
+    } else {  // element-wise, a warp on 32 consecutive states of one row
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+            float f[32];
+#pragma unroll
+            for (int m = 0; m < 32; ++m) {
+                const int idx = et + 256 * (32 * h + m), r = idx >> 7, n = idx & 127, c = r & 63;
+                const int pw = h ? pt.s[1].pw : pt.s[0].pw;
+                f[m] = c < pw ? __ldg(src[h] + (int64_t)c * rs + n) : 0.0f;
+            }
+#pragma unroll
+            for (int m = 0; m < 32; ++m) {
+                const int idx = et + 256 * (32 * h + m), r = idx >> 7, n = idx & 127;
+                st[st_word(r, n)] = f[m];
             }
         }
     }
 }
 
-// Run-entry state for W_c thread `row` (state n): channels p0..p0+63 of
-// s0[ids[seq]] (first run) or of the carry kernel's slot (later runs).
-__device__ __forceinline__ void load_state_row(const ScanParams& p, const OutTile& ot, int row, float (&v)[64]) {
-    const float* src;
-    int64_t sc;
-    if (ot.tl.run == 0) {
-        const int sq = p.has_ids ? p.ids[ot.tl.seq] : ot.tl.seq;
-        src = p.s0 + (int64_t)sq * p.seq_s + (int64_t)ot.tl.h * p.s_s0 + (int64_t)ot.p0 * p.s_s1 + row;
-        sc = p.s_s1;
-    } else {
-        src = p.agg + (ot.unit0 + ot.tl.run - 1) * (int64_t)p.P * p.N + (int64_t)ot.p0 * p.N + row;
-        sc = p.N;
+// s1 of both slabs from st (st_word layout), coalesced.
+__device__ __forceinline__ void store_state_tile(const ScanParams& p, const PairTile& pt, const float* st, int et) {
+#pragma unroll 4
+    for (int m = 0; m < 64; ++m) {
+        const int idx = et + 256 * m, r = idx >> 7, n = idx & 127;
+        const SlabRef sr = (m >> 5) ? pt.s[1] : pt.s[0];
+        const int c = r & 63;
+        if (c < sr.pw)
+            p.s1[(int64_t)pt.seq * p.seq_s + (int64_t)sr.h * p.s_s0 + (int64_t)(sr.p0 + c) * p.s_s1 + n] = st[st_word(r, n)];
     }
-#pragma unroll
-    for (int k = 0; k < 64; ++k) v[k] = k < ot.pw ? src[(int64_t)k * sc] : 0.0f;
 }
 
-__device__ __forceinline__ void out_fast(const TcMaps& maps, const CUtensorMap& ymap, int y_tma, const ScanParams& p,
-                                         const OutTile& ot, uint8_t* sm, uint32_t tm, uint64_t* cb_bar,
-                                         const float (&pre)[64]) {
-    float* ring = reinterpret_cast<float*>(sm + OF_V);
-    __shared__ FastBars bars;
+__device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p, const PairTile& pt, uint8_t* sm,
+                                         uint32_t tm, uint64_t* cb_bar, const float (&pre)[4 * kPV]) {
+    float* ring = reinterpret_cast<float*>(sm + OP_V);
+    __shared__ PairBars bars;
+    __shared__ int cb_issued, cb_landed;  // chunks whose C/B load was issued / waited for
 
-    HX_PHASE_START;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int row = 32 * (warp & 3) + lane;
-    const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-    const Tile tl = ot.tl;
-    const int p0 = ot.p0, pw = ot.pw, n_ch = ot.n_ch;
-    const int t_begin = ot.t_begin, t_end = ot.t_end;
-
-    uint8_t* sS = sm + OF_S;
-    auto sCB = [&](int i) { return sm + OO_CB + (uint32_t)(i & 1) * 65536u; };
-    auto sXW = [&](int i) { return sm + OF_XW + (uint32_t)(i & 1) * 32768u; };
-    auto slot = [&](int i) { return ring + (i % kFRing) * kFVec; };
-    auto vpar = [&](int i) { return (uint32_t)((i / kFRing) & 1); };
-    auto bpar = [&](int i) { return (uint32_t)((i >> 1) & 1); };  // per-buffer parity of chunk i
+    const int n_ch = pt.n_ch, t_begin = pt.t_begin, t_end = pt.t_end;
+    auto slot = [&](int i) { return ring + (i % kPRing) * kPVec; };
+    auto vpar = [&](int i) { return (uint32_t)((i / kPRing) & 1); };
 
     if (tid == 0) {
-        for (int k = 0; k < 2; ++k) {
-            mbar_init(&bars.xw_ready[k], kXwWarps);
-            mbar_init(&bars.xw_free[k], 1);
-            mbar_init(&bars.acc1[k], 1);
-            mbar_init(&bars.g2[k], 1);
-            mbar_init(&bars.d_free[k], 4);
-        }
-        mbar_init(&bars.m_ready, 4);
-        mbar_init(&bars.g4, 1);
-        mbar_init(&bars.d4_ready, 4);
-        mbar_init(&bars.s_ready, 4);
+        mbar_init(&bars.s_ready, kPEpi);
+        mbar_init(&bars.y_free, kPEpi);
+        mbar_init(&bars.m_ready, kPEpi);
+        mbar_init(&bars.d1_free, kPEpi);
+        mbar_init(&bars.xw_ready, kPBld);
+        mbar_init(&bars.s1_ready, kPEpi);
         mbar_init(&bars.g3, 1);
-        for (int k = 0; k < kFRing; ++k) {
+        mbar_init(&bars.g4, 1);
+        mbar_init(&bars.g2, 1);
+        mbar_init(&bars.fin, 1);
+        for (int k = 0; k < kPRing; ++k) {
             mbar_init(&bars.v_full[k], 1);
-            mbar_init(&bars.v_empty[k], 4 + 4 + kXwWarps);  // W_y, W_c, W_xw
+            mbar_init(&bars.v_empty[k], kPBld + kPEpi);
         }
+        cb_issued = n_ch < 2 ? n_ch : 2;  // chunks 0 and 1: the kernel prologue
+        cb_landed = 0;
         fence_mbar_init();
     }
     __syncthreads();
     bool ok = true;
 
-    if (warp == kWarpMma) {
+    if (warp == kPWarpMma) {
         // ================= TMA producer + MMA issuer ========================
         if (lane == 0) {
-            const uint32_t aS = smem_u32(sS);
-            const uint64_t dSm = sdesc_sw128(aS, 16384, 1024);
-            // G1 of chunk k -> D1[k & 1].  D1[k & 1] holds the mask of chunk
-            // k-2 (W_m packs it in place), read by G2(k-2): wait for that first.
+            const uint32_t aCB = smem_u32(sm + OO_CB), aXH = smem_u32(sm + OP_XW), aXL = aXH + 32768;
+            const uint64_t dXh = sdesc_sw128(aXH, 16384, 1024), dXl = sdesc_sw128(aXL, 16384, 1024);
+            int landed = 0;  // C/B chunks waited for
+            // G1 of chunk k -> D1 once its C/B landed and the epilogue has read
+            // D1(k-1); its completion is signalled by the next G3's commit
             auto issue_g1 = [&](int k) -> bool {
-                if (!mbar_wait(&cb_bar[k & 1], bpar(k), kWaitBudget)) return false;
-                if (k >= 2 && !mbar_wait(&bars.g2[k & 1], bpar(k - 2), kWaitBudget)) return false;
-                HX_TL(0, k);
+                if (!mbar_wait(&cb_bar[k & 1], (uint32_t)((k >> 1) & 1), kWaitBudget)) return false;
+                landed = k + 1;
+                if (k >= 1 && !mbar_wait(&bars.d1_free, (uint32_t)((k - 1) & 1), kWaitBudget)) return false;
                 tc_fence_after();
-                const uint32_t aC = smem_u32(sCB(k)), aB = aC + 32768;
-                const uint64_t dCk = sdesc_sw128(aC, 16, 1024), dBk = sdesc_sw128(aB, 16, 1024);
-                const uint32_t tD1 = tm + 128u * (uint32_t)(k & 1);
+                const uint32_t aC = aCB + 65536u * (uint32_t)(k & 1);
+                const uint64_t dC = sdesc_sw128(aC, 16, 1024), dB = sdesc_sw128(aC + 32768, 16, 1024);
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16(tD1, desc_add(dCk, kmajor_off(ks)), desc_add(dBk, kmajor_off(ks)), ID_G1, ks > 0);
-                mma_commit(&bars.acc1[k & 1]);
-                HX_TL(1, k);
+                    mma_bf16(tm + TP_D1, desc_add(dC, kmajor_off(ks)), desc_add(dB, kmajor_off(ks)), ID_P_KK, ks > 0);
                 return true;
             };
-            HX_PHASE_T(1, kMmaTid);
             if (n_ch > 0) ok = issue_g1(0);
-            // Issue order for chunk i: G4(i), G3(i), G1(i+1), G2(i).  G1 runs a
-            // chunk ahead so the tensor pipe has queued work while G2(i) waits
-            // for the mask of chunk i, and W_m gets a chunk of slack.
             for (int i = 0; i < n_ch && ok; ++i) {
-                const int b = i & 1;
                 const uint32_t par = (uint32_t)(i & 1);
-                const uint32_t aC = smem_u32(sCB(i)), aB = aC + 32768, aX = smem_u32(sXW(i));
-                const uint32_t tD = tm + TF_D + 64u * (uint32_t)b;
-                const uint64_t dCk = sdesc_sw128(aC, 16, 1024);
-                const uint64_t dBm = sdesc_sw128(aB, 16384, 1024), dXm = sdesc_sw128(aX, 16384, 1024);
-                // G4 accumulates onto S~_i, which W_c left in D4
-                if (!(ok = mbar_wait(&bars.xw_ready[b], bpar(i), kWaitBudget))) break;
-                if (!(ok = mbar_wait(&bars.d4_ready, par, kWaitBudget))) break;
-                HX_TL(2, i);
-                HX_PHASE_T(3, kMmaTid);
-                tc_fence_after();
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16(tm + TF_D4, desc_add(dBm, 2048u * ks), desc_add(dXm, 2048u * ks), ID_G4N, 1u);
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16(tm + TF_D4, desc_add(dBm, 2048u * ks), desc_add(dXm, 16384u + 2048u * ks), ID_G4N, 1u);
-                mma_commit(&bars.g4);
-                HX_TL(3, i);
+                const uint32_t aC = aCB + 65536u * (uint32_t)(i & 1);
+                const uint64_t dC = sdesc_sw128(aC, 16, 1024);              // C, then the mask (K-major)
+                const uint64_t dBm = sdesc_sw128(aC + 32768, 16384, 1024);  // B as MN-major
                 if (!(ok = mbar_wait(&bars.s_ready, par, kWaitBudget))) break;
-                if (i >= 2) {
-                    if (!(ok = mbar_wait(&bars.d_free[b], bpar(i - 2), kWaitBudget))) break;
-                }
-                HX_TL(4, i);
-                HX_PHASE_T(4, kMmaTid);
+                HX_TL(0, i);
+                if (i >= 1 && !(ok = mbar_wait(&bars.y_free, (uint32_t)((i - 1) & 1), kWaitBudget))) break;
+                HX_TL(1, i);
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16(tD, desc_add(dCk, kmajor_off(ks)), desc_add(dSm, 2048u * ks), ID_G3, ks > 0);
+                    mma_bf16_ts(tm + TP_Y, tm + TP_S + 8u * (uint32_t)ks, desc_add(dC, kmajor_off(ks)), ID_P_KK, ks > 0);
                 mma_commit(&bars.g3);
-                HX_TL(5, i);
-                if (i + 1 < n_ch && !(ok = issue_g1(i + 1))) break;
-                if (!(ok = mbar_wait(&bars.m_ready, par, kWaitBudget))) break;
-                HX_TL(6, i);
-                HX_PHASE_T(5, kMmaTid);
+                HX_TL(2, i);
+                if (!(ok = mbar_wait(&bars.xw_ready, par, kWaitBudget))) break;
+                HX_TL(3, i);
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    mma_bf16_ts(tD, tm + 128u * (uint32_t)b + 8u * (uint32_t)ks, desc_add(dXm, 2048u * ks), ID_G2, 1u);
-                mma_commit(&bars.g2[b]);
+                    mma_bf16(tm + TP_D4, desc_add(dXh, 2048u * ks), desc_add(dBm, 2048u * ks), ID_P_MM, 1u);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                    mma_bf16(tm + TP_D4, desc_add(dXl, 2048u * ks), desc_add(dBm, 2048u * ks), ID_P_MM, 1u);
+                mma_commit(&bars.g4);
+                HX_TL(4, i);
+                if (!(ok = mbar_wait(&bars.m_ready, par, kWaitBudget))) break;
+                HX_TL(5, i);
+                tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks)
+                    mma_bf16(tm + TP_Y, desc_add(dXh, 2048u * ks), desc_add(dC, kmajor_off(ks)), ID_P_MK, 1u);
+                mma_commit(&bars.g2);
+                HX_TL(6, i);
+                if (i + 1 < n_ch && !(ok = issue_g1(i + 1))) break;
                 HX_TL(7, i);
-                // G1(i), G4(i) and G3(i) were the last readers of C/B[b]
-                if (!(ok = mbar_wait(&bars.g3, par, kWaitBudget))) break;
-                if (i + 2 < n_ch) load_cb_chunk(maps, sCB(i + 2), &cb_bar[b], ot.g, t_begin + (i + 2) * kCS, tl.seq);
-                HX_TL(8, i);
-                HX_PHASE_T(6, kMmaTid);
+                if (i + 2 < n_ch) {
+                    // G2(i) was the last reader of chunk i's stage (mask over C, B)
+                    if (!(ok = mbar_wait(&bars.g2, par, kWaitBudget))) break;
+                    HX_TL(8, i);
+                    load_cb_chunk(maps, sm + OO_CB + 65536u * (uint32_t)(i & 1), &cb_bar[i & 1], pt.g,
+                                  t_begin + (i + 2) * kCS, pt.seq);
+                    cb_issued = i + 3;
+                }
             }
-            if (!ok) {
-                atomicCAS(&g_tc_fault, 0u, kFaultMmaOut);
-                mbar_wait(&bars.g3, 0, kWaitBudget);
-            }
+            if (!ok) atomicCAS(&g_tc_fault, 0u, kFaultMmaOut);
+            cb_landed = landed;
         }
         __syncwarp();
-    } else if (warp == kWarpVec) {
-        // ================= chunk vectors ====================================
-        const float Ah2 = ot.Ah * kLog2e;
-        float raw[4] = {pre[0], pre[1], pre[2], pre[3]}, raw_next[4];  // chunk 0 prefetched
-        for (int i = 0; i < n_ch && ok; ++i) {
-            const int t0 = t_begin + i * kCS;
-            if (i + 1 < n_ch) warp_load_dt(p, ot.db, t0 + kCS, t_end, raw_next);
-            float v[4], lc[4], total;
-            warp_chunk_prefix(p, ot.db, t0, min(kCS, t_end - t0), Ah2, raw, v, lc, &total);
-            if (i >= kFRing) {
-                if (!(ok = mbar_wait(&bars.v_empty[i % kFRing], vpar(i - kFRing), kWaitBudget))) break;
-            }
-            float* vs = slot(i);
+    } else if (warp == kPWarpVec) {
+        // ================= chunk vectors of both slabs =======================
+        // raw dt of chunk i+3 is loaded while chunk i is processed and parked
+        // in a private shared-memory ring (no register rotation to wait on)
+        float* dtr = reinterpret_cast<float*>(sm + OP_DT);  // [4][2][128]
+        const float A2[2] = {pt.s[0].Ah * kLog2e, pt.s[1].Ah * kLog2e};
+        auto park = [&](int c, const float (&r0)[4], const float (&r1)[4]) {
+            float* d = dtr + (c & 3) * 256;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const int t = 4 * lane + k;
-                vs[t] = v[k] * ex2(total - lc[k]);
-                vs[128 + t] = ex2(lc[k] - total);
+                d[4 * lane + k] = r0[k];
+                d[128 + 4 * lane + k] = r1[k];
             }
-            if (lane == 0) vs[256] = ex2(total);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars.v_full[i % kFRing]);
-            if (lane == 0) HX_TL(20, i);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) raw[k] = raw_next[k];
+        };
+        {
+            const float r0[4] = {pre[0], pre[1], pre[2], pre[3]}, r1[4] = {pre[4], pre[5], pre[6], pre[7]};
+            park(0, r0, r1);  // chunk 0 prefetched by the kernel prologue
         }
-        if (!ok) atomicCAS(&g_tc_fault, 0u, kFaultMmaOut);
-    } else if (warp >= kWarpXw) {
-        // ================= W_xw: xw = w x, hi | lo ===========================
-        const int r = 32 * xw_index(warp) + lane;
-        const bool leader = r == 0;
-        uint4 cur[kXwVec], nxt[kXwVec];  // chunk 0 was prefetched by the kernel prologue
+        for (int c = 1; c < 3 && c < n_ch; ++c) {
+            float r0[4], r1[4];
+            warp_load_dt(p, pt.s[0].db, t_begin + c * kCS, t_end, r0);
+            warp_load_dt(p, pt.s[1].db, t_begin + c * kCS, t_end, r1);
+            park(c, r0, r1);
+        }
+        __syncwarp();
+#pragma unroll 1
+        for (int i = 0; i < n_ch && ok; ++i) {
+            const int t0 = t_begin + i * kCS;
+            float n0[4], n1[4];
+            const bool more = i + 3 < n_ch;
+            if (more) {
+                warp_load_dt(p, pt.s[0].db, t0 + 3 * kCS, t_end, n0);
+                warp_load_dt(p, pt.s[1].db, t0 + 3 * kCS, t_end, n1);
+            }
+            if (i >= kPRing && !(ok = warp_wait(&bars.v_empty[i % kPRing], vpar(i - kPRing)))) break;
+            if (lane == 0) HX_TL(30, i);
+            float* vs = slot(i);
+#pragma unroll 1
+            for (int v = 0; v < 2; ++v) {
+                const float* d = dtr + (i & 3) * 256 + 128 * v;
+                const float raw[4] = {d[4 * lane], d[4 * lane + 1], d[4 * lane + 2], d[4 * lane + 3]};
+                float dv[4], lc[4], total;
+                warp_chunk_prefix(p, 0, t0, min(kCS, t_end - t0), A2[v], raw, dv, lc, &total);
 #pragma unroll
-        for (int k = 0; k < kXwVec; ++k)
+                for (int k = 0; k < 4; ++k) {
+                    const int t = 4 * lane + k;
+                    vs[kPSlot * v + t] = dv[k] * ex2(total - lc[k]);
+                    vs[kPSlot * v + 128 + t] = ex2(lc[k] - total);
+                }
+                if (lane == 0) vs[kPSlot * v + 256] = ex2(total);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.v_full[i % kPRing]);
+            if (lane == 0) HX_TL(21, i);
+            if (more) park(i + 3, n0, n1);
+            __syncwarp();
+        }
+    } else if (warp >= kPEpi) {
+        // ================= builders: xw = w x, bf16 hi | lo ==================
+        const int r = 32 * bld_index(warp) + lane;
+        uint8_t* xh = sm + OP_XW;
+        uint4 cur[kPV], nxt[kPV];
+#pragma unroll
+        for (int k = 0; k < kPV; ++k)
             cur[k] = make_uint4(__float_as_uint(pre[4 * k]), __float_as_uint(pre[4 * k + 1]),
                                 __float_as_uint(pre[4 * k + 2]), __float_as_uint(pre[4 * k + 3]));
+#pragma unroll 1
         for (int i = 0; i < n_ch; ++i) {
-            if (i + 1 < n_ch) load_x_chunk(p, ot, r, i + 1, nxt);
-            if (!(ok = group_wait(&bars.v_full[i % kFRing], vpar(i), 5, kXwThreads, leader))) break;
-            if (i >= 2) {
-                if (!(ok = group_wait(&bars.xw_free[i & 1], bpar(i - 2), 5, kXwThreads, leader))) break;
-            }
-            if (leader) HX_TL(18, i);
-            HX_PHASE_T(7, 32 * 12);
+            // x of chunk i+1 is requested now and taken over after chunk i is
+            // out, by when it has landed
+            if (i + 1 < n_ch) load_x_pair(p, pt, r, i + 1, nxt);
+            if (!(ok = warp_wait(&bars.v_full[i % kPRing], vpar(i)))) break;
+            if (r == 0) HX_TL(16, i);
+            // lo(i-1) was read by G4(i-1) only; before chunk 0, the epilogue
+            // reads the span-entry state staged over these buffers
+            if (!(ok = i >= 1 ? warp_wait(&bars.g4, (uint32_t)((i - 1) & 1)) : warp_wait(&bars.s_ready, 0u))) break;
+            if (r == 0) HX_TL(17, i);
             const float* wv = slot(i);
-            uint8_t* xh = sXW(i);
 #pragma unroll
-            for (int k = 0; k < kXwVec; ++k) {
-                const int idx = r + kXwThreads * k, j = idx >> 3, c = idx & 7;
-                if (idx < 1024) {
-                    const uint32_t off = sw128_off(j, c);
-                    const float wj = wv[j];
-                    const uint32_t in[4] = {cur[k].x, cur[k].y, cur[k].z, cur[k].w};
+            for (int k = 0; k < kPV; ++k) {
+                const int idx = r + kPBldThreads * k, j = idx >> 4, sl = (idx >> 3) & 1, c = idx & 7;
+                if (idx < 2048) {
+                    const float wj = wv[kPSlot * sl + j];
+                    const bool xv = x_valid(pt, idx, i);
+                    const uint32_t in[4] = {xv ? cur[k].x : 0u, xv ? cur[k].y : 0u, xv ? cur[k].z : 0u,
+                                            xv ? cur[k].w : 0u};
                     uint32_t hi[4], lo[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        float a, bb;
-                        unpack_bf16x2(in[e], a, bb);
+                        float a, b;
+                        unpack_bf16x2(in[e], a, b);
                         a *= wj;
-                        bb *= wj;
-                        hi[e] = pack_bf16x2(a, bb);
+                        b *= wj;
+                        hi[e] = pack_bf16x2(a, b);
                         float ah, bh;
                         unpack_bf16x2(hi[e], ah, bh);
-                        lo[e] = pack_bf16x2(a - ah, bb - bh);
+                        lo[e] = pack_bf16x2(a - ah, b - bh);
                     }
-                    *reinterpret_cast<uint4*>(xh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                    *reinterpret_cast<uint4*>(xh + 16384 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    *reinterpret_cast<uint4*>(xh + 32768u + 16384u * sl + sw128_off(j, c)) =
+                        make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    cur[k] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                 }
+            }
+            if (r == 0) HX_TL(18, i);
+            // hi(i-1) was read by G4(i-1) and G2(i-1)
+            if (i >= 1 && !(ok = warp_wait(&bars.g2, (uint32_t)((i - 1) & 1)))) break;
+            if (r == 0) HX_TL(19, i);
+#pragma unroll
+            for (int k = 0; k < kPV; ++k) {
+                const int idx = r + kPBldThreads * k, j = idx >> 4, sl = (idx >> 3) & 1, c = idx & 7;
+                if (idx < 2048) *reinterpret_cast<uint4*>(xh + 16384u * sl + sw128_off(j, c)) = cur[k];
             }
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&bars.xw_ready[i & 1]);
-                mbar_arrive(&bars.v_empty[i % kFRing]);
+                mbar_arrive(&bars.xw_ready);
+                mbar_arrive(&bars.v_empty[i % kPRing]);
             }
-            if (leader) HX_TL(19, i);
+            if (r == 0) HX_TL(20, i);
 #pragma unroll
-            for (int k = 0; k < kXwVec; ++k) cur[k] = nxt[k];
-            HX_PHASE_T(8, 32 * 12);
-        }
-    } else if (warp >= kWarpC) {
-        // ================= W_c: the carry, in the G4 accumulator ===========
-        const bool leader = tid == 32 * kWarpC;
-        const uint32_t tD4 = tm + lane_off + TF_D4;
-        // S~ = decay S -> D4 (fp32) and bf16 pairs for the smem copy
-        auto scale_store = [&](float (&v)[64], float decay, uint32_t (&sb)[32]) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-#pragma unroll
-                for (int k = 0; k < 16; ++k) v[16 * q + k] *= decay;
-                tmem_st16(tD4 + 16 * q, *reinterpret_cast<const uint32_t(*)[16]>(v + 16 * q));
-#pragma unroll
-                for (int k = 0; k < 8; ++k) sb[8 * q + k] = pack_bf16x2(v[16 * q + 2 * k], v[16 * q + 2 * k + 1]);
-            }
-            tmem_wait_st();
-        };
-        auto store_sbf = [&](const uint32_t (&sb)[32]) {
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                *reinterpret_cast<uint4*>(sS + sw128_off(row, c)) =
-                    make_uint4(sb[4 * c], sb[4 * c + 1], sb[4 * c + 2], sb[4 * c + 3]);
-            fence_async_smem();
-        };
-        // S~_0 from the prefetched run-entry state
-        if (n_ch > 0 && (ok = group_wait(&bars.v_full[0], 0u, 4, 128, leader))) {
-            float v[64];
-#pragma unroll
-            for (int k = 0; k < 64; ++k) v[k] = pre[k];
-            uint32_t sb[32];
-            scale_store(v, slot(0)[256], sb);
-            store_sbf(sb);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&bars.d4_ready);
-                mbar_arrive(&bars.s_ready);
-                mbar_arrive(&bars.v_empty[0]);
-            }
-        }
-        for (int i = 0; i < n_ch && ok; ++i) {
-            const bool last = i + 1 == n_ch;
-            if (!(ok = group_wait(&bars.g4, (uint32_t)(i & 1), 4, 128, leader))) break;
-            float decay = 1.0f;
-            if (!last) {
-                if (!(ok = group_wait(&bars.v_full[(i + 1) % kFRing], vpar(i + 1), 4, 128, leader))) break;
-                decay = slot(i + 1)[256];
-            }
-            if (leader) HX_TL(11, i);
-            HX_PHASE_T(9, 32 * kWarpC);
-            tc_fence_after();
-            float v[64];  // S_{i+1}
-#pragma unroll
-            for (int q = 0; q < 4; ++q) tmem_ld16(tD4 + 16 * q, *reinterpret_cast<float(*)[16]>(v + 16 * q));
-            tmem_wait_ld();
-            if (last) {
-                if (tl.run == p.n_runs - 1) {
-                    float* s1 = p.s1 + (int64_t)tl.seq * p.seq_s + (int64_t)tl.h * p.s_s0 + (int64_t)p0 * p.s_s1 + row;
-#pragma unroll
-                    for (int k = 0; k < 64; ++k)
-                        if (k < pw) s1[(int64_t)k * p.s_s1] = v[k];
-                }
-                break;
-            }
-            uint32_t sb[32];
-            scale_store(v, decay, sb);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&bars.d4_ready);
-                mbar_arrive(&bars.v_empty[(i + 1) % kFRing]);
-            }
-            if (leader) HX_TL(12, i);
-            // smem S~ is G3(i)'s operand: overwrite it once G3(i) retires
-            if (!(ok = group_wait(&bars.g3, (uint32_t)(i & 1), 4, 128, leader))) break;
-            if (leader) HX_TL(13, i);
-            store_sbf(sb);
-            warp_arrive(&bars.s_ready);
-            if (leader) HX_TL(14, i);
-            HX_PHASE_T(10, 32 * kWarpC);
-        }
-    } else if (warp >= kWarpM) {
-        // ================= W_m: causal mask, bf16 pairs into M =============
-        const bool leader = tid == 32 * kWarpM;
-        const int qw = warp & 3;
-        const int rmax = 32 * qw + 31;  // last row of this lane quarter
-        for (int i = 0; i < n_ch; ++i) {
-            if (!(ok = group_wait(&bars.acc1[i & 1], bpar(i), 3, 128, leader))) break;
-            if (leader) HX_TL(9, i);
-            HX_PHASE_T(11, 32 * kWarpM);
-            tc_fence_after();
-            // The mask goes in place: packed pairs over D1[i&1]'s first 64
-            // columns.  Each thread owns its row, and the columns a pass writes
-            // (32 half .. +31) were read in this or the previous pass.  Columns
-            // are read 64 at a time, and only where some row of this lane
-            // quarter needs them.
-            const uint32_t src = tm + lane_off + 128u * (uint32_t)(i & 1);
-            const uint32_t dst = src;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                if (64 * half <= rmax) {
-                    float d[64];
-#pragma unroll
-                    for (int g = 0; g < 4; ++g)
-                        if (64 * half + 16 * g <= rmax)
-                            tmem_ld16(src + 64 * half + 16 * g, *reinterpret_cast<float(*)[16]>(d + 16 * g));
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int h2 = 0; h2 < 2; ++h2) {
-                        uint32_t mp[16];
-#pragma unroll
-                        for (int e2 = 0; e2 < 16; ++e2) {
-                            const int e = 16 * h2 + e2;
-                            const int j = 64 * half + 2 * e;
-                            const bool need = 64 * half + 16 * (e >> 3) <= rmax;
-                            mp[e2] = need ? pack_bf16x2(j <= row ? d[2 * e] : 0.0f, j + 1 <= row ? d[2 * e + 1] : 0.0f)
-                                          : 0u;
-                        }
-                        tmem_st16(dst + 32 * half + 16 * h2, mp);
-                    }
-                } else {
-                    const uint32_t z[16] = {};
-                    tmem_st16(dst + 32 * half, z);
-                    tmem_st16(dst + 32 * half + 16, z);
-                }
-            }
-            tmem_wait_st();
-            tc_fence_before();
-            warp_arrive(&bars.m_ready);
-            if (leader) HX_TL(10, i);
-            HX_PHASE_T(12, 32 * kWarpM);
+            for (int k = 0; k < kPV; ++k) cur[k] = nxt[k];
         }
     } else {
-        // ================= W_y: y = f_t D ==================================
-        // D[i&1] is read whole and released at once; y goes out through the
-        // xw buffer of the same chunk (free once G2 retired) and two TMA
-        // stores, after which the buffer is handed back to W_xw.
-        const bool leader = tid == 0;
-        for (int i = 0; i < n_ch; ++i) {
-            if (!(ok = group_wait(&bars.g2[i & 1], bpar(i), 2, 128, leader))) break;
-            if (!(ok = group_wait(&bars.v_full[i % kFRing], vpar(i), 2, 128, leader))) break;
-            if (leader) HX_TL(15, i);
-            HX_PHASE(13);
-            tc_fence_after();
+        // ================= epilogue =========================================
+        const int q = warp & 3, kh = warp >> 2;
+        const int lane_row = 32 * q + lane;  // t for D1 / mask, slab channel for Y, D4, S~
+        const uint32_t lo = (uint32_t)(32 * q) << 16;
+        const int v = q >> 1;
+        const SlabRef sr = v ? pt.s[1] : pt.s[0];
+        const int c = lane_row & 63;
+        const bool c_ok = c < sr.pw;
+        const uint32_t col = 64u * (uint32_t)kh;
+        const int rmax = 32 * q + 31;  // last row (t) of this lane quarter
+        // D1 of the chunk -> causal mask for rows t, columns 64 kh .. +63
+        auto build_mask = [&](uint32_t (&mk)[32]) {
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+                const int j0 = 64 * kh + 32 * h2;
+                if (j0 <= rmax) {
+                    float d[32];
+                    tmem_ld16(tm + lo + TP_D1 + col + 32 * h2, *reinterpret_cast<float(*)[16]>(d));
+                    tmem_ld16(tm + lo + TP_D1 + col + 32 * h2 + 16, *reinterpret_cast<float(*)[16]>(d + 16));
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int j = j0 + 2 * e;
+                        mk[16 * h2 + e] = pack_bf16x2(j <= lane_row ? d[2 * e] : 0.0f, j + 1 <= lane_row ? d[2 * e + 1] : 0.0f);
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) mk[16 * h2 + e] = 0u;
+                }
+            }
+            tc_fence_before();
+            warp_arrive(&bars.d1_free);
+        };
+        // S~ = decay S -> D4 (fp32) and its bf16 pairs -> S~ columns, for the
+        // 32 state columns 32 h2 .. +31 of this thread's half
+        auto put_state32 = [&](float (&s)[32], int h2, float decay) {
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                uint32_t f[16], b[8];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    s[16 * g + k] *= decay;
+                    f[k] = __float_as_uint(s[16 * g + k]);
+                }
+#pragma unroll
+                for (int k = 0; k < 8; ++k) b[k] = pack_bf16x2(s[16 * g + 2 * k], s[16 * g + 2 * k + 1]);
+                tmem_st16(tm + lo + TP_D4 + col + 32 * h2 + 16 * g, f);
+                tmem_st8(tm + lo + TP_S + 32 * kh + 16 * h2 + 8 * g, b);
+            }
+        };
+        if (n_ch > 0 && (ok = warp_wait(&bars.v_full[0], 0u))) {
+            // the span-entry state, staged by the kernel prologue over the xw
+            // buffers (the builders wait for s_ready before their first store)
+            const float* st = reinterpret_cast<const float*>(sm + OP_XW);
+            const float e0 = slot(0)[kPSlot * v + 256];
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+                float s[32];
+#pragma unroll
+                for (int k = 0; k < 32; ++k) s[k] = st[st_word(lane_row, 64 * kh + 32 * h2 + k)];
+                put_state32(s, h2, e0);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            warp_arrive(&bars.s_ready);
+        }
+        for (int i = 0; i < n_ch && ok; ++i) {
+            const uint32_t par = (uint32_t)(i & 1);
             const int tp = t_begin + i * kCS;
             const int tlen = t_end - tp;
-            const float f = slot(i)[128 + row];
-            float a[64];
+            // (1) the mask of D1(i), written over C(i) once G3(i) (and G1(i)
+            // before it) retired
+            if (!(ok = warp_wait(&bars.g3, par))) break;
+            if (tid == 0) HX_TL(9, i);
+            tc_fence_after();
+            {
+                uint32_t mk[32];
+                build_mask(mk);
+                uint8_t* ms = sm + OO_CB + 65536u * (uint32_t)(i & 1) + 16384u * (uint32_t)kh;
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                tmem_ld16(tm + lane_off + TF_D + 64u * (uint32_t)(i & 1) + 16 * q, *reinterpret_cast<float(*)[16]>(a + 16 * q));
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&bars.d_free[i & 1]);
-                mbar_arrive(&bars.v_empty[i % kFRing]);
-            }
-            if (leader) HX_TL(16, i);
-            if (y_tma) {
-                uint8_t* stg = sXW(i);
-#pragma unroll
-                for (int c = 0; c < 16; ++c)
-                    *reinterpret_cast<float4*>(stg + 16384 * (c >> 3) + sw128_off(row, c & 7)) =
-                        make_float4(f * a[4 * c], f * a[4 * c + 1], f * a[4 * c + 2], f * a[4 * c + 3]);
+                for (int c8 = 0; c8 < 8; ++c8)
+                    *reinterpret_cast<uint4*>(ms + sw128_off(lane_row, c8)) =
+                        make_uint4(mk[4 * c8], mk[4 * c8 + 1], mk[4 * c8 + 2], mk[4 * c8 + 3]);
                 fence_async_smem();
-                named_sync(2, 128);
-                if (leader) {
-                    tma_store_4d(&ymap, stg, p0, tl.h, tp, tl.seq);
-                    if (p0 + 32 < p.P) tma_store_4d(&ymap, stg + 16384, p0 + 32, tl.h, tp, tl.seq);
-                    bulk_commit();
-                    bulk_wait_read0();  // the staging tiles have been read
-                    mbar_arrive(&bars.xw_free[i & 1]);
-                    HX_TL(17, i);
-                }
-            } else {
-                if (row < tlen) {
-                    float* yr = p.y + (int64_t)tl.seq * p.seq_y + (int64_t)(tp + row) * p.s_y0 +
-                                (int64_t)tl.h * p.s_y1 + (int64_t)p0 * p.s_y2;
-#pragma unroll
-                    for (int k = 0; k < 64; ++k)
-                        if (k < pw) yr[(int64_t)k * p.s_y2] = f * a[k];
-                }
-                if (leader) mbar_arrive(&bars.xw_free[i & 1]);
+                warp_arrive(&bars.m_ready);
+                if (tid == 0) HX_TL(10, i);
             }
-            HX_PHASE(14);
+            // (2) S_{i+1} from D4 (the last chunk's state is read once y has left)
+            if (!(ok = warp_wait(&bars.g4, par))) break;
+            if (tid == 0) HX_TL(11, i);
+            const bool last = i + 1 == n_ch;
+            if (!last && !(ok = warp_wait(&bars.v_full[(i + 1) % kPRing], vpar(i + 1)))) break;
+            tc_fence_after();
+            if (!last) {
+                const float decay = slot(i + 1)[kPSlot * v + 256];
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    float s[32];
+                    tmem_ld16(tm + lo + TP_D4 + col + 32 * h2, *reinterpret_cast<float(*)[16]>(s));
+                    tmem_ld16(tm + lo + TP_D4 + col + 32 * h2 + 16, *reinterpret_cast<float(*)[16]>(s + 16));
+                    tmem_wait_ld();
+                    put_state32(s, h2, decay);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                warp_arrive(&bars.s_ready);
+                if (tid == 0) HX_TL(12, i);
+            }
+            // (3) y(i) = f_t Y
+            if (!(ok = warp_wait(&bars.g2, par))) break;
+            if (tid == 0) HX_TL(13, i);
+            tc_fence_after();
+            {
+                float a[64];
+#pragma unroll
+                for (int g = 0; g < 4; ++g) tmem_ld16(tm + lo + TP_Y + col + 16 * g, *reinterpret_cast<float(*)[16]>(a + 16 * g));
+                tmem_wait_ld();
+                tc_fence_before();
+                warp_arrive(&bars.y_free);
+                if (tid == 0) HX_TL(14, i);
+                // one 128-byte row (32 channels) per store
+                const float4* f4 = reinterpret_cast<const float4*>(slot(i) + kPSlot * v + 128 + 64 * kh);
+                if (c_ok) {
+                    float* yp = p.y + (int64_t)pt.seq * p.seq_y + (int64_t)(tp + 64 * kh) * p.s_y0 +
+                                (int64_t)sr.h * p.s_y1 + (int64_t)(sr.p0 + c) * p.s_y2;
+                    const int64_t sy = p.s_y0;
+                    const int kmax = tlen - 64 * kh;
+#pragma unroll
+                    for (int k4 = 0; k4 < 16; ++k4) {
+                        const float4 fv = f4[k4];
+                        const float fk[4] = {fv.x, fv.y, fv.z, fv.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            if (4 * k4 + e < kmax) *yp = fk[e] * a[4 * k4 + e];
+                            yp += sy;
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars.v_empty[i % kPRing]);
+                if (tid == 0) HX_TL(15, i);
+                if (lane == 0) HX_TL(22 + warp, i);
+            }
         }
-        if (leader && y_tma) bulk_wait0();  // y stores complete before the CTA exits
+        if (ok && pt.last && n_ch > 0) {
+            // s1 = D4 after the last G4, through the xw buffers (every MMA has
+            // retired: this warp saw the last G2 complete)
+            float* st1 = reinterpret_cast<float*>(sm + OP_XW);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+                float s[32];
+                tmem_ld16(tm + lo + TP_D4 + col + 32 * h2, *reinterpret_cast<float(*)[16]>(s));
+                tmem_ld16(tm + lo + TP_D4 + col + 32 * h2 + 16, *reinterpret_cast<float(*)[16]>(s + 16));
+                tmem_wait_ld();
+#pragma unroll
+                for (int k = 0; k < 32; ++k) st1[st_word(lane_row, 64 * kh + 32 * h2 + k)] = s[k];
+            }
+            warp_arrive(&bars.s1_ready);
+            if ((ok = warp_wait(&bars.s1_ready, 0u))) store_state_tile(p, pt, st1, tid);
+        }
+    }
+    // drain: every MMA retired and every C/B load landed before the CTA
+    // releases its tensor memory and shared memory
+    __syncthreads();
+    if (tid == kPMmaTid) {
+        mma_commit(&bars.fin);
+        mbar_wait(&bars.fin, 0u, kWaitBudget);
+        for (int k = cb_landed; k < cb_issued; ++k) mbar_wait(&cb_bar[k & 1], (uint32_t)((k >> 1) & 1), kWaitBudget);
     }
 }
 
 // ---------------------------------------------------------------------------
-// Output kernel entry: shared prologue, then one of the two paths for the
-// whole CTA.  The prologue allocates TMEM, starts the C/B loads of chunks 0
-// and 1 (same smem layout and barriers in both paths) and, while they fly,
-// measures the largest per-chunk decay of the run.
+// Output kernels.  A pair tile runs the fast path (tc_out_kernel) unless one
+// of its chunks decays by more than kFastSpan2, P is not a multiple of 8, or
+// HELIX_TC_GENERAL asks for the general path; such tiles are left to
+// tc_out_general_kernel, launched right after.  The fast kernel records its
+// decision per tile in the scratch (multipass); without scratch the general
+// kernel takes the same decision with the same code on the same data (the
+// decay span of every chunk of both slabs, maxed), so each tile is done
+// exactly once.  Two kernels keep the two paths' register allocations apart.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(kOutThreads, 1)
-    tc_out_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ CUtensorMap ymap, ScanParams p,
-                  int y_tma, int force_general) {
+// Largest per-chunk decay span |A| sum_t dt_t (log2 units) over both slabs of
+// the span, one warp per (chunk, slab) unit, maxed into *span_bits.  Called
+// by `nw` warps, warp index `wi` (0 .. nw-1).
+__device__ __forceinline__ void pair_span(const ScanParams& p, const PairTile& pt, int wi, int nw, unsigned* span_bits) {
+    const int lane = threadIdx.x & 31;
+    float mx = 0.0f;
+    for (int u = wi; u < 2 * pt.n_ch; u += nw) {
+        const SlabRef sr = (u & 1) ? pt.s[1] : pt.s[0];
+        const int t0 = pt.t_begin + (u >> 1) * kCS;
+        float raw[4];
+        warp_load_dt(p, sr.db, t0, pt.t_end, raw);
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (t0 + 4 * lane + k < pt.t_end) sum += dt_of(raw[k], p.dt_min, p.dt_max);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        mx = fmaxf(mx, sum * fabsf(sr.Ah) * kLog2e);
+    }
+    if (lane == 0 && mx > 0.0f) atomicMax(span_bits, __float_as_uint(mx));
+}
+__device__ __forceinline__ bool pair_takes_fast(const ScanParams& p, unsigned span_bits, int force_general) {
+    return !force_general && (p.P & 7) == 0 && __uint_as_float(span_bits) <= kFastSpan2;
+}
+
+// Fast path.  The prologue allocates TMEM, starts the C/B loads of chunks 0
+// and 1 and, while they fly, measures the decay span and prefetches the
+// first inputs: the span-entry state tile (epilogue warps, into shared
+// memory), x of chunk 0 (builders), dt of chunk 0 (vector warp).
+__global__ void __launch_bounds__(kPThreads, 1)
+    tc_out_kernel(const __grid_constant__ TcMaps maps, ScanParams p, int force_general) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
     __shared__ uint64_t cb_bar[2];
@@ -1164,7 +1319,7 @@ __global__ void __launch_bounds__(kOutThreads, 1)
     __shared__ unsigned span_bits;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const OutTile ot = out_tile(p);
+    const PairTile pt = pair_tile(p);
     if (tid == 0) HX_TL(31, 0);
     if (tid == 0) {
         mbar_init(&cb_bar[0], 1);
@@ -1172,82 +1327,126 @@ __global__ void __launch_bounds__(kOutThreads, 1)
         span_bits = 0u;
         fence_mbar_init();
     }
-    if (warp == kWarpMma) {
+    if (warp == kPWarpMma) {
         tmem_alloc(&tmem_base, 512);
         tmem_relinquish();
     }
     __syncthreads();
     tc_fence_after();
-    if (tid == kMmaTid) {
+    if (tid == kPMmaTid) {
         prefetch_tmap(&maps.x);
         prefetch_tmap(&maps.b);
         prefetch_tmap(&maps.c);
-        if (y_tma) prefetch_tmap(&ymap);
-        for (int i = 0; i < 2 && i < ot.n_ch; ++i)
-            load_cb_chunk(maps, sm + OO_CB + (uint32_t)i * 65536u, &cb_bar[i], ot.g, ot.t_begin + i * kCS, ot.tl.seq);
+        for (int i = 0; i < 2 && i < pt.n_ch; ++i)
+            load_cb_chunk(maps, sm + OO_CB + (uint32_t)i * 65536u, &cb_bar[i], pt.g, pt.t_begin + i * kCS, pt.seq);
     }
-    // While the C/B loads fly: W_y and W_m warps measure each chunk's decay
-    // span (|A| sum_t dt_t, log2 units, one warp per chunk) and the other
-    // fast-path roles prefetch their first inputs into pre[]: the run-entry
-    // state (W_c), x of chunk 0 (W_xw), dt of chunk 0 (vector warp).
-    float pre[64];
-    if (warp < kWarpC) {
-        const float aa = fabsf(ot.Ah) * kLog2e;
-        float mx = 0.0f;
-        for (int c = warp; c < ot.n_ch; c += kWarpC) {
-            const int t0 = ot.t_begin + c * kCS;
+    float pre[4 * kPV];  // x of chunk 0 (builders) or dt of chunk 0 (vector warp)
+    float* st = reinterpret_cast<float*>(sm + OP_XW);  // free until the builders start
+    if (warp < kPEpi) {
+        load_state_tile(p, pt, st, tid);
+    } else if (warp == kPWarpVec) {
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
             float raw[4];
-            warp_load_dt(p, ot.db, t0, ot.t_end, raw);
-            float sum = 0.0f;
+            warp_load_dt(p, pt.s[v].db, pt.t_begin, pt.t_end, raw);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                if (t0 + 4 * lane + k < ot.t_end) sum += dt_of(raw[k], p.dt_min, p.dt_max);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            mx = fmaxf(mx, sum * aa);
+            for (int k = 0; k < 4; ++k) pre[4 * v + k] = raw[k];
         }
-        if (lane == 0 && mx > 0.0f) atomicMax(&span_bits, __float_as_uint(mx));
-    } else if (warp < kWarpXw) {
-        load_state_row(p, ot, 32 * (warp & 3) + lane, pre);
-    } else if (warp != kWarpMma && warp != kWarpVec) {
-        uint4 v[kXwVec];
-        load_x_chunk(p, ot, 32 * xw_index(warp) + lane, 0, v);
+    } else if (warp != kPWarpMma) {
+        uint4 v[kPV];
+        load_x_pair(p, pt, 32 * bld_index(warp) + lane, 0, v);
 #pragma unroll
-        for (int k = 0; k < kXwVec; ++k) {
+        for (int k = 0; k < kPV; ++k) {
             pre[4 * k] = __uint_as_float(v[k].x);
             pre[4 * k + 1] = __uint_as_float(v[k].y);
             pre[4 * k + 2] = __uint_as_float(v[k].z);
             pre[4 * k + 3] = __uint_as_float(v[k].w);
         }
-    } else if (warp == kWarpVec) {
-        float raw[4];
-        warp_load_dt(p, ot.db, ot.t_begin, ot.t_end, raw);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) pre[k] = raw[k];
+        pair_span(p, pt, bld_index(warp), kPBld, &span_bits);
     }
     __syncthreads();
     if (tid == 0) HX_TL(31, 1);
     const uint32_t tm = tmem_base;
-    if (!force_general && __uint_as_float(span_bits) <= kFastSpan2)
-        out_fast(maps, ymap, y_tma, p, ot, sm, tm, cb_bar, pre);
-    else
-        out_general(maps, p, ot, sm, tm, cb_bar);
+    const bool fast = pair_takes_fast(p, span_bits, force_general);
+    if (tid == 0 && p.tile_flag) p.tile_flag[blockIdx.x] = fast ? 1 : 0;
+    if (!fast) {
+        // the general kernel does this tile: let the C/B loads land first
+        if (tid == kPMmaTid)
+            for (int i = 0; i < 2 && i < pt.n_ch; ++i) mbar_wait(&cb_bar[i], 0u, kWaitBudget);
+        __syncthreads();
+        if (warp == kPWarpMma) tmem_dealloc(tm, 512);
+        return;
+    }
+    out_pair(maps, p, pt, sm, tm, cb_bar, pre);
     tc_fence_before();
     __syncthreads();
-    if (warp == kWarpMma) {
+    if (warp == kPWarpMma) {
         tc_fence_after();
         tmem_dealloc(tm, 512);
     }
 }
 
+// General path: one CTA per tile the fast kernel left, its slabs one after
+// the other (each with its own barriers).
+__global__ void __launch_bounds__(kOutThreads, 1)
+    tc_out_general_kernel(const __grid_constant__ TcMaps maps, ScanParams p, int force_general) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = align1024(smem_raw);
+    __shared__ uint64_t cb_bar[4];
+    __shared__ uint32_t tmem_base;
+    __shared__ unsigned span_bits;
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const PairTile pt = pair_tile(p);
+    if (tid == 0) {
+        for (int k = 0; k < 4; ++k) mbar_init(&cb_bar[k], 1);
+        span_bits = 0u;
+        fence_mbar_init();
+    }
+    if (p.tile_flag) {  // the fast kernel's record
+        if (p.tile_flag[blockIdx.x]) return;
+    } else {
+        __syncthreads();
+        pair_span(p, pt, warp, kOutThreads / 32, &span_bits);
+        __syncthreads();
+        if (pair_takes_fast(p, span_bits, force_general)) return;
+    }
+    if (warp == kGWarpMma) {
+        tmem_alloc(&tmem_base, 512);
+        tmem_relinquish();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = tmem_base;
+#pragma unroll 1
+    for (int v = 0; v < 2; ++v) {
+        if (!pt.s[v].valid) continue;
+        if (tid == 32 * kGWarpMma) {
+            if (v == 0) {
+                prefetch_tmap(&maps.x);
+                prefetch_tmap(&maps.b);
+                prefetch_tmap(&maps.c);
+            }
+            for (int i = 0; i < 2 && i < pt.n_ch; ++i)
+                load_cb_chunk(maps, sm + OO_CB + (uint32_t)i * 65536u, &cb_bar[2 * v + i], pt.g, pt.t_begin + i * kCS,
+                              pt.seq);
+        }
+        out_general(maps, p, slab_tile(pt, v), sm, tm, cb_bar + 2 * v, v);
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
+    if (warp == kGWarpMma) tmem_dealloc(tm, 512);
+}
 
 // ---------------------------------------------------------------------------
 // Carry kernel (the reference's Pass B, over runs instead of chunks): turns
-// the run states from a zero start into run-entry states, in place:
-//   S = s0[ids[seq]];  for r = 0 .. R-2:  S = exp(lam_r) S + agg_r;  agg_r <- S
-// so afterwards slot r holds the state entering run r + 1.  One thread per
-// float4 of one (seq, head)'s [P][N] state; the loads of successive runs are
-// independent, so several are kept in flight.
+// the run states from a zero start into span-entry states, in place:
+//   S = s0[ids[seq]];  for r < state_runs:  S = exp(lam_r) S + agg_r;
+//   agg_r <- S  where run r + 1 starts an output span ((r + 1) % out_k == 0)
+// so afterwards slot k*out_k - 1 holds the state entering span k.  One thread
+// per float4 of one (seq, head)'s [P][N] state; the loads of successive runs
+// are independent, so several are kept in flight.
 // ---------------------------------------------------------------------------
 constexpr int kCarryThreads = 256;
 
@@ -1262,9 +1461,9 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
     const int src = p.has_ids ? p.ids[seq] : seq;
     const float* s0 = p.s0 + (int64_t)src * p.seq_s + (int64_t)h * p.s_s0 + (int64_t)c * p.s_s1 + n;
     float4 S = make_float4(s0[0], s0[1], s0[2], s0[3]);
-    const int64_t unit0 = head_lin * p.n_runs;
+    const int64_t unit0 = head_lin * p.run_slots;
     float4* agg = reinterpret_cast<float4*>(p.agg + unit0 * (int64_t)p.P * p.N) + e4;
-    const int R = p.n_runs - 1;
+    const int R = p.state_runs, K = p.out_k;
     int r = 0;
     for (; r + 4 <= R; r += 4) {
         float4 v[4];
@@ -1280,7 +1479,7 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
             S.y = fmaf(a[k], S.y, v[k].y);
             S.z = fmaf(a[k], S.z, v[k].z);
             S.w = fmaf(a[k], S.w, v[k].w);
-            agg[(r + k) * per_head4] = S;
+            if ((r + k + 1) % K == 0) agg[(r + k) * per_head4] = S;
         }
     }
     for (; r < R; ++r) {
@@ -1290,7 +1489,7 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
         S.y = fmaf(a, S.y, v.y);
         S.z = fmaf(a, S.z, v.z);
         S.w = fmaf(a, S.w, v.w);
-        agg[r * per_head4] = S;
+        if ((r + 1) % K == 0) agg[r * per_head4] = S;
     }
 }
 
@@ -1527,7 +1726,7 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
             ok = st_wait(&bars.xw_empty[(n_st - 1) & 1], (uint32_t)(((n_st - 1) >> 1) & 1), kFaultMmaState);
         tc_fence_after();
         if (ok) {
-            const int64_t unit = ((int64_t)tl.seq * p.H + tl.h) * p.n_runs + tl.run;
+            const int64_t unit = ((int64_t)tl.seq * p.H + tl.h) * p.run_slots + tl.run;
             float* out = p.agg + unit * (int64_t)p.P * p.N + (int64_t)p0 * p.N + row;
             // columns 0..63 hold the hi part, 64..127 the lo part
 #pragma unroll
@@ -1547,7 +1746,7 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
     tc_fence_before();
     __syncthreads();
     if (ok && tid == 0 && tl.slab == 0)
-        p.lam[((int64_t)tl.seq * p.H + tl.h) * p.n_runs + tl.run] = lam_total;
+        p.lam[((int64_t)tl.seq * p.H + tl.h) * p.run_slots + tl.run] = lam_total;
     if (is_mma) {
         tc_fence_after();
         tmem_dealloc(tm, 128);
@@ -1575,34 +1774,12 @@ bool make_map(EncodeFn fn, CUtensorMap* m, const void* base, int64_t inner, int6
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// 4-D f32 map (chan, head, tok, seq) for TMA stores of y, box 32 x 1 x 128 x 1,
-// 128-byte swizzle.  Rows past L and channels past P are not written.
-bool make_ymap(EncodeFn fn, CUtensorMap* m, void* base, const ScanParams& p) {
-    cuuint64_t dims[4] = {(cuuint64_t)p.P, (cuuint64_t)p.H, (cuuint64_t)p.L, (cuuint64_t)p.S};
-    cuuint64_t strides[3] = {(cuuint64_t)(p.s_y1 * 4), (cuuint64_t)(p.s_y0 * 4), (cuuint64_t)(p.seq_y * 4)};
-    cuuint32_t box[4] = {32, 1, (cuuint32_t)kCS, 1};
-    cuuint32_t es[4] = {1, 1, 1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// TMA stores of y need unit channel stride, 16-byte multiples for the other
-// strides and a 16-byte aligned base.
 // Maps of the state kernel: x and B in 64-token boxes (its step).
 bool make_state_maps(EncodeFn fn, TcMaps* m, const ScanParams& p) {
     const int64_t S = p.S;
     std::memset(&m->c, 0, sizeof(m->c));
     return make_map(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf) &&
            make_map(fn, &m->b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf);
-}
-
-bool y_tma_ok(const ScanParams& p) {
-    if (p.s_y2 != 1) return false;
-    const int64_t st[3] = {p.s_y1, p.s_y0, p.seq_y};
-    for (int64_t s : st)
-        if (s <= 0 || (s * 4) % 16 != 0) return false;
-    return (reinterpret_cast<uintptr_t>(p.y) & 15) == 0;
 }
 
 // Test hook: HELIX_TC_GENERAL=1 sends every CTA of the output kernel down
@@ -1616,6 +1793,8 @@ int force_general() {
 
 int configure_tc(const helix_ctx*) {
     cudaError_t e = cudaFuncSetAttribute(tc_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_OUT);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(tc_out_general_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_OUT);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(tc_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_STATE);
 }
@@ -1632,17 +1811,13 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* s
         !make_map(fn, &maps.b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b) ||
         !make_map(fn, &maps.c, p.C, p.N, p.G, p.L, S, p.s_c1, p.s_c0, p.seq_c))
         return cudaErrorInvalidValue;
-    CUtensorMap ymap;
-    int y_tma = y_tma_ok(p) ? 1 : 0;
-    if (y_tma && !make_ymap(fn, &ymap, p.y, p)) y_tma = 0;
-    if (!y_tma) std::memset(&ymap, 0, sizeof(ymap));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const char* only = std::getenv("HELIX_ONLY_PASS");
     const bool do_a = !only || *only == 'A';
     const bool do_c = !only || *only == 'C';
     const int64_t per_run = (int64_t)p.n_pslab * p.H * S;
     if (pl.need_state_kernel && do_a) {
-        const int runs = pl.n_runs - 1;
+        const int runs = pl.state_runs;
         TcMaps smaps;
         if (!make_state_maps(fn, &smaps, p)) return cudaErrorInvalidValue;
         tc_state_kernel<<<(unsigned)(per_run * runs), kStThreads, SMEM_STATE, st>>>(smaps, p, runs);
@@ -1657,8 +1832,13 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* s
         if (e != cudaSuccess) return e;
     }
     if (do_c) {
-        tc_out_kernel<<<(unsigned)(per_run * pl.n_runs), kOutThreads, SMEM_OUT, st>>>(maps, ymap, p, y_tma, force_general());
-        const cudaError_t e = cudaGetLastError();
+        const int64_t ctas = (int64_t)S * p.G * p.n_pair * p.n_out;
+        const int fg = force_general();
+        tc_out_kernel<<<(unsigned)ctas, kPThreads, SMEM_OUT, st>>>(maps, p, fg);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        tc_out_general_kernel<<<(unsigned)ctas, kOutThreads, SMEM_OUT, st>>>(maps, p, fg);
+        e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
@@ -1671,8 +1851,8 @@ int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, 
     const int64_t S = p.S;
     if (!make_state_maps(fn, &maps, p)) return cudaErrorInvalidValue;
     const int64_t per_run = (int64_t)p.n_pslab * p.H * S;
-    tc_state_kernel<<<(unsigned)(per_run * pl.n_runs), kStThreads, SMEM_STATE, static_cast<cudaStream_t>(stream)>>>(
-        maps, p, pl.n_runs);
+    tc_state_kernel<<<(unsigned)(per_run * pl.state_runs), kStThreads, SMEM_STATE, static_cast<cudaStream_t>(stream)>>>(
+        maps, p, pl.state_runs);
     return cudaGetLastError();
 }
 

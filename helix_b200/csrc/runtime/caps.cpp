@@ -98,6 +98,53 @@ bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why) 
     return true;
 }
 
+namespace {
+
+// Run cut of the tensor-core family.  Its output kernel gives a CTA two
+// 64-channel slabs of one group (a "pair") over a span of consecutive runs,
+// so the span length is picked first: the one that minimises (waves of
+// CTAs) x (blocks per span + half a block of start-up).  The span is then
+// cut into runs fine enough that the state kernel (two CTAs per SM) has
+// about four CTAs per SM to spread over.
+void tc_split(const helix_scan_desc& d, int blocks, int n_sm, int max_runs, int* run_blocks, int* out_k) {
+    const int64_t units = (int64_t)(d.n_head / d.n_group) * ((d.head_dim + kSlab - 1) / kSlab);
+    const int64_t pairs = (int64_t)d.n_seq * d.n_group * ((units + 1) / 2);
+    double best = 1e300;
+    int sb = blocks;
+    for (int n = 1; n <= blocks; ++n) {
+        const int b = (blocks + n - 1) / n;
+        if ((blocks + b - 1) / b != n) continue;  // same span length as a smaller n
+        const int64_t waves = (pairs * n + n_sm - 1) / n_sm;
+        const double cost = (double)waves * (b + 0.5);
+        if (cost < best) {
+            best = cost;
+            sb = b;
+        }
+    }
+    const int n_out = (blocks + sb - 1) / sb;
+    int k = 1;
+    if (n_out > 1) {
+        const int64_t st_units = (int64_t)d.n_seq * d.n_head * ((d.head_dim + kSlab - 1) / kSlab) * (n_out - 1);
+        const int64_t want = std::max<int64_t>(1, (4 * (int64_t)n_sm + st_units - 1) / st_units);
+        k = sb;
+        for (int c = 1; c <= sb; ++c)
+            if (sb % c == 0 && c >= want) {
+                k = c;
+                break;
+            }
+        // stay within the run-slot budget
+        while (k > 1 && (int64_t)(blocks + sb / k - 1) / (sb / k) > max_runs) {
+            int c = k - 1;
+            while (c > 1 && sb % c != 0) --c;
+            k = c;
+        }
+    }
+    *run_blocks = sb / k;
+    *out_k = k;
+}
+
+}  // namespace
+
 Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     Plan pl;
     pl.path = select_path(d);
@@ -105,31 +152,46 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     pl.n_pslab = (d.head_dim + kSlab - 1) / kSlab;
 
     const int blocks = (d.n_tok + kRunQuantum - 1) / kRunQuantum;  // 128-token blocks
-    int n_runs = 1;
+    const int n_sm = ctx ? std::max(ctx->n_sm, 1) : 148;
+    const size_t per_run = (size_t)d.n_seq * d.n_head * d.head_dim * d.d_state * sizeof(float);
+    const int max_runs = (int)std::min<size_t>((size_t)kMaxRuns,
+                                               std::max<size_t>(1, scratch_budget() / std::max<size_t>(per_run, 1)));
+    int run_blocks = blocks, out_k = 1;
     if (d.multipass) {
-        // Enough CTAs in the output kernel to cover every SM a few times.
-        const int64_t units = (int64_t)d.n_seq * d.n_head * pl.n_pslab;
-        const int64_t target = 4 * (int64_t)(ctx ? std::max(ctx->n_sm, 1) : 148);
-        n_runs = (int)std::min<int64_t>(blocks, std::max<int64_t>(1, (target + units - 1) / units));
-        const size_t per_run = (size_t)d.n_seq * d.n_head * d.head_dim * d.d_state * sizeof(float);
-        const size_t cap = std::max<size_t>(1, scratch_budget() / std::max<size_t>(per_run, 1));
-        n_runs = (int)std::min<size_t>((size_t)n_runs, cap);
-    }
-    int run_blocks = (blocks + n_runs - 1) / n_runs;
-    if (d.multipass) {
-        if (const int f = forced_run_tokens()) run_blocks = std::max(1, f / kRunQuantum);
+        if (const int f = forced_run_tokens()) {
+            run_blocks = std::max(1, f / kRunQuantum);
+        } else if (pl.path == kPathTcBf16) {
+            tc_split(d, blocks, n_sm, max_runs, &run_blocks, &out_k);
+        } else {
+            // Enough CTAs in the output kernel to cover every SM a few times.
+            const int64_t units = (int64_t)d.n_seq * d.n_head * pl.n_pslab;
+            const int64_t target = 4 * (int64_t)n_sm;
+            int n_runs = (int)std::min<int64_t>(blocks, std::max<int64_t>(1, (target + units - 1) / units));
+            n_runs = std::min(n_runs, max_runs);
+            run_blocks = (blocks + n_runs - 1) / n_runs;
+        }
     }
     run_blocks = std::max(run_blocks, (blocks + kMaxRuns - 1) / kMaxRuns);
     pl.run_tok = run_blocks * kRunQuantum;
     pl.n_runs = (blocks + run_blocks - 1) / run_blocks;
-    pl.need_state_kernel = pl.n_runs > 1;
+    pl.out_k = std::max(1, std::min(out_k, pl.n_runs));
+    pl.n_out = (pl.n_runs + pl.out_k - 1) / pl.out_k;
+    pl.state_runs = pl.out_k * (pl.n_out - 1);
+    pl.run_slots = pl.state_runs;
+    pl.need_state_kernel = pl.state_runs > 0;
 
-    if (pl.n_runs > 1) {
-        const size_t agg = (size_t)d.n_seq * d.n_head * pl.n_runs * d.head_dim * d.d_state;
-        const size_t lam = (size_t)d.n_seq * d.n_head * pl.n_runs;
+    // The tensor-core output kernels record per tile which path ran, so the
+    // general-path kernel need not re-measure the decay spans.
+    pl.has_flags = d.multipass && pl.path == kPathTcBf16;
+    if (pl.run_slots > 0 || pl.has_flags) {
+        const size_t agg = (size_t)d.n_seq * d.n_head * pl.run_slots * d.head_dim * d.d_state;
+        const size_t lam = (size_t)d.n_seq * d.n_head * pl.run_slots;
+        const int64_t units = (int64_t)(d.n_head / d.n_group) * pl.n_pslab;
+        const size_t tiles = pl.has_flags ? (size_t)d.n_seq * d.n_group * ((units + 1) / 2) * pl.n_out : 0;
         pl.off_agg = 0;
         pl.off_lam = align256(agg * sizeof(float));
-        pl.total = pl.off_lam + align256(lam * sizeof(float));
+        pl.off_flag = pl.off_lam + align256(lam * sizeof(float));
+        pl.total = pl.off_flag + align256(tiles * sizeof(int32_t));
     }
     return pl;
 }
@@ -138,13 +200,16 @@ Plan make_shard_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     helix_scan_desc m = d;
     m.multipass = true;
     Plan pl = make_plan(ctx, m);
-    if (pl.total == 0) {  // a single run: make_plan keeps no slots for it
-        const size_t agg = (size_t)d.n_seq * d.n_head * pl.n_runs * d.head_dim * d.d_state;
-        const size_t lam = (size_t)d.n_seq * d.n_head * pl.n_runs;
-        pl.off_agg = 0;
-        pl.off_lam = align256(agg * sizeof(float));
-        pl.total = pl.off_lam + align256(lam * sizeof(float));
-    }
+    // every run's state is reduced (the fold needs them all)
+    pl.state_runs = pl.n_runs;
+    pl.run_slots = pl.n_runs;
+    pl.need_state_kernel = true;
+    pl.has_flags = false;
+    const size_t agg = (size_t)d.n_seq * d.n_head * pl.run_slots * d.head_dim * d.d_state;
+    const size_t lam = (size_t)d.n_seq * d.n_head * pl.run_slots;
+    pl.off_agg = 0;
+    pl.off_lam = align256(agg * sizeof(float));
+    pl.total = pl.off_lam + align256(lam * sizeof(float));
     return pl;
 }
 

@@ -109,6 +109,7 @@ helix_status encode_core(helix_ctx* ctx, void* stream, const helix_scan_desc* d,
     if (pl.total > 0) {
         p.agg = reinterpret_cast<float*>(at<char>(scratch) + pl.off_agg);
         p.lam = reinterpret_cast<float*>(at<char>(scratch) + pl.off_lam);
+        p.tile_flag = pl.has_flags ? reinterpret_cast<int32_t*>(at<char>(scratch) + pl.off_flag) : nullptr;
     }
 
     if (pl.path == hx::kPathTcBf16) {
@@ -150,6 +151,14 @@ void fill_params(ScanParams& p, const helix_scan_desc& d, const Plan& pl) {
     p.n_pslab = pl.n_pslab;
     p.run_tok = pl.run_tok;
     p.n_runs = pl.n_runs;
+    p.out_k = pl.out_k;
+    p.n_out = pl.n_out;
+    p.state_runs = pl.state_runs;
+    p.run_slots = pl.run_slots;
+    {
+        const int units = p.hpg * p.n_pslab;
+        p.n_pair = (units + 1) / 2;
+    }
     p.io_bf16 = d.io_dtype == HELIX_BF16 ? 1 : 0;
     p.dt_min = d.dt_min;
     p.dt_max = d.dt_max;

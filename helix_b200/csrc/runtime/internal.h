@@ -45,9 +45,19 @@ struct Plan {
     int    run_tok  = 0;    // tokens per run (multiple of kRunQuantum)
     int    n_runs   = 1;
     int    n_pslab  = 1;
-    bool   need_state_kernel = false;  // n_runs > 1
-    size_t off_agg  = 0;    // f32 [seq][head][run][head_dim][d_state]
-    size_t off_lam  = 0;    // f32 [seq][head][run]
+    // The output kernel gives each CTA out_k consecutive runs (a "span"):
+    // n_out spans per sequence.  The state kernel reduces the runs before the
+    // last span (state_runs of them); their states sit in run_slots slots
+    // per (seq, head).
+    int    out_k      = 1;
+    int    n_out      = 1;
+    int    state_runs = 0;
+    int    run_slots  = 0;
+    bool   need_state_kernel = false;  // state_runs > 0
+    size_t off_agg  = 0;    // f32 [seq][head][run_slots][head_dim][d_state]
+    size_t off_lam  = 0;    // f32 [seq][head][run_slots]
+    size_t off_flag = 0;    // i32 [output tiles] (tensor-core family, multipass): fast path taken
+    bool   has_flags = false;
     size_t total    = 0;    // scratch bytes
 };
 
@@ -55,6 +65,8 @@ struct Plan {
 struct ScanParams {
     int32_t S, L, H, P, N, G, hpg;
     int32_t n_pslab, run_tok, n_runs;
+    int32_t out_k, n_out, state_runs, run_slots;   // see Plan
+    int32_t n_pair;         // two-slab tiles per group: ceil(hpg * n_pslab / 2)
     int32_t has_ids;
     int32_t io_bf16;        // x, B, C stored as bf16
     float   dt_min, dt_max;
@@ -78,6 +90,7 @@ struct ScanParams {
     float*         s1;
     float*         agg;     // scratch, see Plan
     float*         lam;
+    int32_t*       tile_flag;  // scratch or null, see Plan
 };
 
 }  // namespace hx

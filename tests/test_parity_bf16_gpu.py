@@ -29,6 +29,10 @@ SHAPES = [  # reference tests/test_metal_parity.mm:77-104, d_state = 128 rows
     (160, 1, 4, 64, 128, 1), (300, 1, 8, 64, 128, 2), (256, 1, 4, 128, 128, 1),
     (256, 1, 4, 192, 128, 1), (256, 1, 8, 128, 128, 8), (256, 4, 4, 64, 128, 1),
     (1024, 1, 2, 64, 128, 1), (2048, 1, 8, 64, 128, 2), (200, 1, 2, 72, 128, 1),
+    # output tiles pair two slabs of a group: an odd slab count leaves the
+    # last pair half empty; many pairs make the planner give each output CTA
+    # a span of several runs
+    (192, 1, 3, 64, 128, 1), (256, 2, 8, 64, 128, 8), (1024, 1, 128, 64, 128, 1),
 ]
 MODES = [("1pass", False, None), ("multipass", True, None), ("multipass/runs128", True, "128")]
 
