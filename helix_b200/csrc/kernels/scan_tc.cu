@@ -44,6 +44,13 @@ extern __device__ unsigned long long hx_phase_cycles[32];
 // Timeline of one CTA (blockIdx.x == HX_TL_CTA): clock64 of event `ev` in
 // chunk `i`.
 extern __device__ long long hx_tl[32 * 64];
+extern __device__ unsigned long long hx_cta[512 * 4];
+__device__ __forceinline__ unsigned long long hx_gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+#define HX_CTA(k) do { if (threadIdx.x == 0 && blockIdx.x < 512) hx_cta[blockIdx.x * 4 + (k)] = hx_gtime(); } while (0)
 #define HX_TL_CTA 40
 #define HX_TL(ev, i)                                                          \
     do {                                                                      \
@@ -51,6 +58,7 @@ extern __device__ long long hx_tl[32 * 64];
     } while (0)
 #else
 #define HX_TL(ev, i) do {} while (0)
+#define HX_CTA(k) do {} while (0)
 #define HX_PHASE_START do {} while (0)
 #define HX_PHASE(k) do {} while (0)
 #define HX_PHASE_T(k, who) do {} while (0)
@@ -776,38 +784,58 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
     return ok;
 }
 
-// x of chunk i for builder thread r: vector idx = r + kPBldThreads k of the
-// chunk's 2048 (token j = idx >> 4, slab (idx >> 3) & 1, channels 8 (idx & 7)
-// .. +7).  The fast path runs only when P is a multiple of 8, so every vector
-// lies inside or outside its slab as a whole.  Vectors are loaded without a
-// condition (ones that do not exist read token t_end - 1 or the tensor's
-// first vector, and x_valid() zeroes them where they are used), so nothing
-// waits for the loads before their use.
-__device__ __forceinline__ bool x_valid(const PairTile& pt, int idx, int i) {
-    const int j = idx >> 4, sl = (idx >> 3) & 1, c = idx & 7;
-    const int pw = sl ? pt.s[1].pw : pt.s[0].pw;
-    return idx < 2048 && pt.t_begin + i * kCS + j < pt.t_end && 8 * c < pw;
+// x of a chunk for builder thread r: its 16-byte vectors idx = r + kPBldThreads k
+// of the chunk's 2048 are token j0 + kJStep k, slab sl, channels 8 c .. +7,
+// with j0 = r >> 4, sl = (r >> 3) & 1 and c = r & 7 the same for every k
+// (kPBldThreads is a multiple of 16), so one row pointer per thread serves all
+// its vectors.  The fast path runs only when P is a multiple of 8, so every
+// vector lies inside or outside its slab as a whole.  Vectors are loaded
+// without a condition on their value (ones that do not exist read the
+// tensor's first vector and are zeroed where they are used), so nothing waits
+// for the loads before their use.
+constexpr int kJStep = kPBldThreads / 16;
+static_assert(kPBldThreads % 16 == 0, "builder vectors keep their slab and channels");
+struct XLane {
+    const __nv_bfloat16* row;  // token 0 of the sequence, this lane's slab and channels
+    int j0, sl, c;
+    bool c_in;                 // channels inside the slab
+};
+__device__ __forceinline__ XLane x_lane(const ScanParams& p, const PairTile& pt, int r) {
+    XLane xl;
+    xl.j0 = r >> 4;
+    xl.sl = (r >> 3) & 1;
+    xl.c = r & 7;
+    const SlabRef sr = xl.sl ? pt.s[1] : pt.s[0];
+    xl.c_in = 8 * xl.c < sr.pw;
+    xl.row = static_cast<const __nv_bfloat16*>(p.x) + (int64_t)pt.seq * p.seq_x + (int64_t)sr.h * p.s_x1 + sr.p0 +
+             8 * xl.c;
+    return xl;
 }
-__device__ __forceinline__ void load_x_pair(const ScanParams& p, const PairTile& pt, int r, int i,
+__device__ __forceinline__ bool x_ok(const XLane& xl, const PairTile& pt, int i, int k) {
+    const int j = xl.j0 + kJStep * k;
+    return xl.c_in && j < kCS && pt.t_begin + i * kCS + j < pt.t_end;
+}
+__device__ __forceinline__ void load_x_pair(const ScanParams& p, const PairTile& pt, const XLane& xl, int i,
                                             uint4 (&v)[kPV]) {
     const __nv_bfloat16* xg = static_cast<const __nv_bfloat16*>(p.x);
+    const __nv_bfloat16* base = xl.row + (int64_t)(pt.t_begin + i * kCS + xl.j0) * p.s_x0;
+    const int64_t step = (int64_t)kJStep * p.s_x0;
 #pragma unroll
-    for (int k = 0; k < kPV; ++k) {
-        const int idx = r + kPBldThreads * k, j = idx >> 4, sl = (idx >> 3) & 1, c = idx & 7;
-        const int t = min(pt.t_begin + i * kCS + j, pt.t_end - 1);
-        const SlabRef sr = sl ? pt.s[1] : pt.s[0];
-        const bool in = idx < 2048 && 8 * c < sr.pw;
-        const __nv_bfloat16* src =
-            xg + (int64_t)pt.seq * p.seq_x + (int64_t)t * p.s_x0 + (int64_t)sr.h * p.s_x1 + sr.p0 + 8 * c;
-        v[k] = __ldg(reinterpret_cast<const uint4*>(in ? src : xg));
-    }
+    for (int k = 0; k < kPV; ++k)
+        v[k] = __ldg(reinterpret_cast<const uint4*>(x_ok(xl, pt, i, k) ? base + k * step : xg));
 }
 
 // State tile of a pair in shared memory: row r = 64 v + c (slab v, channel
-// c), state n at word 128 r + (n ^ (r & 31)).  The XOR keeps both access
-// patterns free of bank conflicts: a warp on 32 consecutive n of one row
-// (global side) and a warp on one n of 32 consecutive rows (TMEM lane side).
-__device__ __forceinline__ uint32_t st_word(int r, int n) { return (uint32_t)(128 * r + (n ^ (r & 31))); }
+// c), 128 states per row, the float4 holding states 4 m .. 4 m + 3 at slot
+// m ^ (r & 7).  The XOR keeps both access patterns at the minimum number of
+// shared-memory wavefronts: a warp on the 32 float4 of one row (global side)
+// and a warp on one float4 slot of 32 consecutive rows (TMEM lane side).
+__device__ __forceinline__ uint32_t st_word(int r, int n) {
+    return (uint32_t)(128 * r + 4 * ((n >> 2) ^ (r & 7)) + (n & 3));
+}
+__device__ __forceinline__ float4* st_vec(float* st, int r, int m) {
+    return reinterpret_cast<float4*>(st + 128 * r + 4 * (m ^ (r & 7)));
+}
 
 // The span-entry states of both slabs -> st (fp32, st_word layout), by the
 // 256 epilogue threads (et = 0..255) with coalesced loads: s0[ids[seq]] for
@@ -836,11 +864,8 @@ __device__ __forceinline__ void load_state_tile(const ScanParams& p, const PairT
             }
 #pragma unroll
             for (int m = 0; m < 8; ++m) {
-                const int i4 = et + 256 * (8 * h + m), r = i4 >> 5, n = 4 * (i4 & 31);
-                st[st_word(r, n)] = f[m].x;
-                st[st_word(r, n + 1)] = f[m].y;
-                st[st_word(r, n + 2)] = f[m].z;
-                st[st_word(r, n + 3)] = f[m].w;
+                const int i4 = et + 256 * (8 * h + m);
+                *st_vec(st, i4 >> 5, i4 & 31) = f[m];
             }
         }
     } else {  // element-wise, a warp on 32 consecutive states of one row
@@ -862,15 +887,26 @@ __device__ __forceinline__ void load_state_tile(const ScanParams& p, const PairT
     }
 }
 
-// s1 of both slabs from st (st_word layout), coalesced.
+// s1 of both slabs from st (st_word layout), coalesced: float4 rows when s1
+// allows it, single states otherwise.
 __device__ __forceinline__ void store_state_tile(const ScanParams& p, const PairTile& pt, const float* st, int et) {
-#pragma unroll 4
-    for (int m = 0; m < 64; ++m) {
-        const int idx = et + 256 * m, r = idx >> 7, n = idx & 127;
-        const SlabRef sr = (m >> 5) ? pt.s[1] : pt.s[0];
-        const int c = r & 63;
-        if (c < sr.pw)
-            p.s1[(int64_t)pt.seq * p.seq_s + (int64_t)sr.h * p.s_s0 + (int64_t)(sr.p0 + c) * p.s_s1 + n] = st[st_word(r, n)];
+    float* const d0 = p.s1 + (int64_t)pt.seq * p.seq_s + (int64_t)pt.s[0].h * p.s_s0 + (int64_t)pt.s[0].p0 * p.s_s1;
+    float* const d1 = p.s1 + (int64_t)pt.seq * p.seq_s + (int64_t)pt.s[1].h * p.s_s0 + (int64_t)pt.s[1].p0 * p.s_s1;
+    const bool vec = (p.s_s1 & 3) == 0 && ((reinterpret_cast<uintptr_t>(d0) | reinterpret_cast<uintptr_t>(d1)) & 15) == 0;
+    if (vec) {
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            const int i4 = et + 256 * m, r = i4 >> 5, c = r & 63;
+            if (c < ((m >> 3) ? pt.s[1].pw : pt.s[0].pw))
+                *reinterpret_cast<float4*>(((m >> 3) ? d1 : d0) + (int64_t)c * p.s_s1 + 4 * (i4 & 31)) =
+                    *reinterpret_cast<const float4*>(st + 128 * r + 4 * ((i4 & 31) ^ (r & 7)));
+        }
+    } else {
+#pragma unroll 1
+        for (int m = 0; m < 64; ++m) {
+            const int idx = et + 256 * m, r = idx >> 7, n = idx & 127, c = r & 63;
+            if (c < ((m >> 5) ? pt.s[1].pw : pt.s[0].pw)) ((m >> 5) ? d1 : d0)[(int64_t)c * p.s_s1 + n] = st[st_word(r, n)];
+        }
     }
 }
 
@@ -979,8 +1015,9 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
         __syncwarp();
     } else if (warp == kPWarpVec) {
         // ================= chunk vectors of both slabs =======================
-        // raw dt of chunk i+3 is loaded while chunk i is processed and parked
-        // in a private shared-memory ring (no register rotation to wait on)
+        // Slot 0 was filled by the kernel prologue.  Raw dt of chunk i+3 is
+        // loaded while chunk i is processed and parked in a private
+        // shared-memory ring (no register rotation to wait on).
         float* dtr = reinterpret_cast<float*>(sm + OP_DT);  // [4][2][128]
         const float A2[2] = {pt.s[0].Ah * kLog2e, pt.s[1].Ah * kLog2e};
         auto park = [&](int c, const float (&r0)[4], const float (&r1)[4]) {
@@ -991,19 +1028,21 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 d[128 + 4 * lane + k] = r1[k];
             }
         };
+        if (lane == 0 && n_ch > 0) mbar_arrive(&bars.v_full[0]);
+        if (lane == 0) HX_TL(21, 0);
         {
-            const float r0[4] = {pre[0], pre[1], pre[2], pre[3]}, r1[4] = {pre[4], pre[5], pre[6], pre[7]};
-            park(0, r0, r1);  // chunk 0 prefetched by the kernel prologue
-        }
-        for (int c = 1; c < 3 && c < n_ch; ++c) {
-            float r0[4], r1[4];
-            warp_load_dt(p, pt.s[0].db, t_begin + c * kCS, t_end, r0);
-            warp_load_dt(p, pt.s[1].db, t_begin + c * kCS, t_end, r1);
-            park(c, r0, r1);
+            float r[3][2][4];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                warp_load_dt(p, pt.s[0].db, t_begin + (c + 1) * kCS, t_end, r[c][0]);
+                warp_load_dt(p, pt.s[1].db, t_begin + (c + 1) * kCS, t_end, r[c][1]);
+            }
+#pragma unroll
+            for (int c = 0; c < 3; ++c) park(c + 1, r[c][0], r[c][1]);
         }
         __syncwarp();
 #pragma unroll 1
-        for (int i = 0; i < n_ch && ok; ++i) {
+        for (int i = 1; i < n_ch && ok; ++i) {
             const int t0 = t_begin + i * kCS;
             float n0[4], n1[4];
             const bool more = i + 3 < n_ch;
@@ -1036,8 +1075,9 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
         }
     } else if (warp >= kPEpi) {
         // ================= builders: xw = w x, bf16 hi | lo ==================
-        const int r = 32 * bld_index(warp) + lane;
-        uint8_t* xh = sm + OP_XW;
+        const XLane xl = x_lane(p, pt, 32 * bld_index(warp) + lane);
+        const bool lead = warp == 8 && lane == 0;
+        uint8_t* xt = sm + OP_XW + 16384u * (uint32_t)xl.sl;  // this slab's hi tile; lo 32 KB on
         uint4 cur[kPV], nxt[kPV];
 #pragma unroll
         for (int k = 0; k < kPV; ++k)
@@ -1047,20 +1087,20 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
         for (int i = 0; i < n_ch; ++i) {
             // x of chunk i+1 is requested now and taken over after chunk i is
             // out, by when it has landed
-            if (i + 1 < n_ch) load_x_pair(p, pt, r, i + 1, nxt);
+            if (i + 1 < n_ch) load_x_pair(p, pt, xl, i + 1, nxt);
             if (!(ok = warp_wait(&bars.v_full[i % kPRing], vpar(i)))) break;
-            if (r == 0) HX_TL(16, i);
+            if (lead) HX_TL(16, i);
             // lo(i-1) was read by G4(i-1) only; before chunk 0, the epilogue
             // reads the span-entry state staged over these buffers
             if (!(ok = i >= 1 ? warp_wait(&bars.g4, (uint32_t)((i - 1) & 1)) : warp_wait(&bars.s_ready, 0u))) break;
-            if (r == 0) HX_TL(17, i);
-            const float* wv = slot(i);
+            if (lead) HX_TL(17, i);
+            const float* wv = slot(i) + kPSlot * xl.sl + xl.j0;
 #pragma unroll
             for (int k = 0; k < kPV; ++k) {
-                const int idx = r + kPBldThreads * k, j = idx >> 4, sl = (idx >> 3) & 1, c = idx & 7;
-                if (idx < 2048) {
-                    const float wj = wv[kPSlot * sl + j];
-                    const bool xv = x_valid(pt, idx, i);
+                const int j = xl.j0 + kJStep * k;
+                if (j < kCS) {
+                    const float wj = wv[kJStep * k];
+                    const bool xv = x_ok(xl, pt, i, k);
                     const uint32_t in[4] = {xv ? cur[k].x : 0u, xv ? cur[k].y : 0u, xv ? cur[k].z : 0u,
                                             xv ? cur[k].w : 0u};
                     uint32_t hi[4], lo[4];
@@ -1075,19 +1115,18 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                         unpack_bf16x2(hi[e], ah, bh);
                         lo[e] = pack_bf16x2(a - ah, b - bh);
                     }
-                    *reinterpret_cast<uint4*>(xh + 32768u + 16384u * sl + sw128_off(j, c)) =
-                        make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    *reinterpret_cast<uint4*>(xt + 32768u + sw128_off(j, xl.c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                     cur[k] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                 }
             }
-            if (r == 0) HX_TL(18, i);
+            if (lead) HX_TL(18, i);
             // hi(i-1) was read by G4(i-1) and G2(i-1)
             if (i >= 1 && !(ok = warp_wait(&bars.g2, (uint32_t)((i - 1) & 1)))) break;
-            if (r == 0) HX_TL(19, i);
+            if (lead) HX_TL(19, i);
 #pragma unroll
             for (int k = 0; k < kPV; ++k) {
-                const int idx = r + kPBldThreads * k, j = idx >> 4, sl = (idx >> 3) & 1, c = idx & 7;
-                if (idx < 2048) *reinterpret_cast<uint4*>(xh + 16384u * sl + sw128_off(j, c)) = cur[k];
+                const int j = xl.j0 + kJStep * k;
+                if (j < kCS) *reinterpret_cast<uint4*>(xt + sw128_off(j, xl.c)) = cur[k];
             }
             fence_async_smem();
             __syncwarp();
@@ -1095,7 +1134,7 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 mbar_arrive(&bars.xw_ready);
                 mbar_arrive(&bars.v_empty[i % kPRing]);
             }
-            if (r == 0) HX_TL(20, i);
+            if (lead) HX_TL(20, i);
 #pragma unroll
             for (int k = 0; k < kPV; ++k) cur[k] = nxt[k];
         }
@@ -1159,7 +1198,13 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             for (int h2 = 0; h2 < 2; ++h2) {
                 float s[32];
 #pragma unroll
-                for (int k = 0; k < 32; ++k) s[k] = st[st_word(lane_row, 64 * kh + 32 * h2 + k)];
+                for (int m = 0; m < 8; ++m) {
+                    const float4 f = *st_vec(const_cast<float*>(st), lane_row, 16 * kh + 8 * h2 + m);
+                    s[4 * m] = f.x;
+                    s[4 * m + 1] = f.y;
+                    s[4 * m + 2] = f.z;
+                    s[4 * m + 3] = f.w;
+                }
                 put_state32(s, h2, e0);
             }
             tmem_wait_st();
@@ -1241,7 +1286,7 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars.v_empty[i % kPRing]);
                 if (tid == 0) HX_TL(15, i);
-                if (lane == 0) HX_TL(22 + warp, i);
+                if (lane == 0 && warp < 2) HX_TL(22 + warp, i);
             }
         }
         if (ok && pt.last && n_ch > 0) {
@@ -1255,7 +1300,8 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 tmem_ld16(tm + lo + TP_D4 + col + 32 * h2 + 16, *reinterpret_cast<float(*)[16]>(s + 16));
                 tmem_wait_ld();
 #pragma unroll
-                for (int k = 0; k < 32; ++k) st1[st_word(lane_row, 64 * kh + 32 * h2 + k)] = s[k];
+                for (int m = 0; m < 8; ++m)
+                    *st_vec(st1, lane_row, 16 * kh + 8 * h2 + m) = make_float4(s[4 * m], s[4 * m + 1], s[4 * m + 2], s[4 * m + 3]);
             }
             warp_arrive(&bars.s1_ready);
             if ((ok = warp_wait(&bars.s1_ready, 0u))) store_state_tile(p, pt, st1, tid);
@@ -1287,18 +1333,29 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
 __device__ __forceinline__ void pair_span(const ScanParams& p, const PairTile& pt, int wi, int nw, unsigned* span_bits) {
     const int lane = threadIdx.x & 31;
     float mx = 0.0f;
-    for (int u = wi; u < 2 * pt.n_ch; u += nw) {
-        const SlabRef sr = (u & 1) ? pt.s[1] : pt.s[0];
-        const int t0 = pt.t_begin + (u >> 1) * kCS;
-        float raw[4];
-        warp_load_dt(p, sr.db, t0, pt.t_end, raw);
-        float sum = 0.0f;
+    // four units' dt in flight at a time
+    for (int u0 = wi; u0 < 2 * pt.n_ch; u0 += 4 * nw) {
+        float raw[4][4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            if (t0 + 4 * lane + k < pt.t_end) sum += dt_of(raw[k], p.dt_min, p.dt_max);
+        for (int b = 0; b < 4; ++b) {
+            const int u = min(u0 + b * nw, 2 * pt.n_ch - 1);
+            const SlabRef sr = (u & 1) ? pt.s[1] : pt.s[0];
+            warp_load_dt(p, sr.db, pt.t_begin + (u >> 1) * kCS, pt.t_end, raw[b]);
+        }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        mx = fmaxf(mx, sum * fabsf(sr.Ah) * kLog2e);
+        for (int b = 0; b < 4; ++b) {
+            const int u = u0 + b * nw;
+            if (u < 2 * pt.n_ch) {
+                const int t0 = pt.t_begin + (u >> 1) * kCS;
+                float sum = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (t0 + 4 * lane + k < pt.t_end) sum += dt_of(raw[b][k], p.dt_min, p.dt_max);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                mx = fmaxf(mx, sum * fabsf((u & 1) ? pt.s[1].Ah : pt.s[0].Ah) * kLog2e);
+            }
+        }
     }
     if (lane == 0 && mx > 0.0f) atomicMax(span_bits, __float_as_uint(mx));
 }
@@ -1309,7 +1366,8 @@ __device__ __forceinline__ bool pair_takes_fast(const ScanParams& p, unsigned sp
 // Fast path.  The prologue allocates TMEM, starts the C/B loads of chunks 0
 // and 1 and, while they fly, measures the decay span and prefetches the
 // first inputs: the span-entry state tile (epilogue warps, into shared
-// memory), x of chunk 0 (builders), dt of chunk 0 (vector warp).
+// memory), x of chunk 0 (builders), the chunk vectors of chunk 0 (vector
+// warp, straight into its ring slot).
 __global__ void __launch_bounds__(kPThreads, 1)
     tc_out_kernel(const __grid_constant__ TcMaps maps, ScanParams p, int force_general) {
     extern __shared__ uint8_t smem_raw[];
@@ -1320,6 +1378,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const PairTile pt = pair_tile(p);
+    HX_CTA(0);
+    grid_dep_launch();  // the general-path kernel waits for this grid anyway
     if (tid == 0) HX_TL(31, 0);
     if (tid == 0) {
         mbar_init(&cb_bar[0], 1);
@@ -1340,21 +1400,37 @@ __global__ void __launch_bounds__(kPThreads, 1)
         for (int i = 0; i < 2 && i < pt.n_ch; ++i)
             load_cb_chunk(maps, sm + OO_CB + (uint32_t)i * 65536u, &cb_bar[i], pt.g, pt.t_begin + i * kCS, pt.seq);
     }
-    float pre[4 * kPV];  // x of chunk 0 (builders) or dt of chunk 0 (vector warp)
+    float pre[4 * kPV];  // x of chunk 0 (builders)
     float* st = reinterpret_cast<float*>(sm + OP_XW);  // free until the builders start
     if (warp < kPEpi) {
+        // launched behind the carry kernel, this kernel may run its prologue
+        // early: everything above reads only the scan's inputs; the carry
+        // kernel's span-entry states are read after the wait
+        grid_dep_wait();
         load_state_tile(p, pt, st, tid);
+        if (tid == 0) HX_TL(24, 0);
+        pair_span(p, pt, warp, kPEpi + kPBld, &span_bits);
+        if (tid == 0) HX_TL(25, 0);
     } else if (warp == kPWarpVec) {
+        // the chunk vectors of chunk 0 straight into ring slot 0
+        float* vs = reinterpret_cast<float*>(sm + OP_V);
+        const int tlen = min(kCS, pt.t_end - pt.t_begin);
 #pragma unroll
         for (int v = 0; v < 2; ++v) {
-            float raw[4];
+            float raw[4], dv[4], lc[4], total;
             warp_load_dt(p, pt.s[v].db, pt.t_begin, pt.t_end, raw);
+            warp_chunk_prefix(p, 0, pt.t_begin, tlen, pt.s[v].Ah * kLog2e, raw, dv, lc, &total);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) pre[4 * v + k] = raw[k];
+            for (int k = 0; k < 4; ++k) {
+                vs[kPSlot * v + 4 * lane + k] = dv[k] * ex2(total - lc[k]);
+                vs[kPSlot * v + 128 + 4 * lane + k] = ex2(lc[k] - total);
+            }
+            if (lane == 0) vs[kPSlot * v + 256] = ex2(total);
         }
+        if (lane == 0) HX_TL(26, 0);
     } else if (warp != kPWarpMma) {
         uint4 v[kPV];
-        load_x_pair(p, pt, 32 * bld_index(warp) + lane, 0, v);
+        load_x_pair(p, pt, x_lane(p, pt, 32 * bld_index(warp) + lane), 0, v);
 #pragma unroll
         for (int k = 0; k < kPV; ++k) {
             pre[4 * k] = __uint_as_float(v[k].x);
@@ -1362,7 +1438,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
             pre[4 * k + 2] = __uint_as_float(v[k].z);
             pre[4 * k + 3] = __uint_as_float(v[k].w);
         }
-        pair_span(p, pt, bld_index(warp), kPBld, &span_bits);
+        pair_span(p, pt, kPEpi + bld_index(warp), kPEpi + kPBld, &span_bits);
+        if (warp == 8 && lane == 0) HX_TL(27, 0);
     }
     __syncthreads();
     if (tid == 0) HX_TL(31, 1);
@@ -1377,9 +1454,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (warp == kPWarpMma) tmem_dealloc(tm, 512);
         return;
     }
+    HX_CTA(1);
     out_pair(maps, p, pt, sm, tm, cb_bar, pre);
     tc_fence_before();
     __syncthreads();
+    HX_CTA(2);
     if (warp == kPWarpMma) {
         tc_fence_after();
         tmem_dealloc(tm, 512);
@@ -1398,6 +1477,7 @@ __global__ void __launch_bounds__(kOutThreads, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const PairTile pt = pair_tile(p);
+    grid_dep_wait();  // the fast kernel's records and outputs
     if (tid == 0) {
         for (int k = 0; k < 4; ++k) mbar_init(&cb_bar[k], 1);
         span_bits = 0u;
@@ -1451,6 +1531,8 @@ __global__ void __launch_bounds__(kOutThreads, 1)
 constexpr int kCarryThreads = 256;
 
 __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
+    grid_dep_wait();    // the state kernel's run states
+    grid_dep_launch();  // the output kernel may start its prologue
     const int64_t per_head4 = (int64_t)p.P * p.N / 4;
     const int64_t gid = (int64_t)blockIdx.x * kCarryThreads + threadIdx.x;
     const int64_t head_lin = gid / per_head4;  // seq * H + h
@@ -1825,20 +1907,36 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* s
         if (e != cudaSuccess) return e;
     }
     const bool do_b = !only || *only == 'B';
-    if (pl.need_state_kernel && do_b) {
+    // Kernels that follow another kernel of this call are launched as
+    // programmatic dependents: their CTAs may start while the previous grid
+    // drains and wait (griddepcontrol.wait) before reading its results.
+    auto launch = [&](auto kernel, unsigned grid, unsigned block, size_t smem, bool after_ours, auto... args) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(block);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = after_ours ? 1 : 0;
+        return cudaLaunchKernelEx(&cfg, kernel, args...);
+    };
+    const bool state_ran = pl.need_state_kernel && do_a;
+    const bool carry_ran = pl.need_state_kernel && do_b;
+    if (carry_ran) {
         const int64_t n4 = (int64_t)S * p.H * p.P * p.N / 4;
-        tc_carry_kernel<<<(unsigned)((n4 + kCarryThreads - 1) / kCarryThreads), kCarryThreads, 0, st>>>(p);
-        const cudaError_t e = cudaGetLastError();
+        const cudaError_t e = launch(tc_carry_kernel, (unsigned)((n4 + kCarryThreads - 1) / kCarryThreads),
+                                     kCarryThreads, 0, state_ran, p);
         if (e != cudaSuccess) return e;
     }
     if (do_c) {
         const int64_t ctas = (int64_t)S * p.G * p.n_pair * p.n_out;
         const int fg = force_general();
-        tc_out_kernel<<<(unsigned)ctas, kPThreads, SMEM_OUT, st>>>(maps, p, fg);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch(tc_out_kernel, (unsigned)ctas, kPThreads, SMEM_OUT, carry_ran, maps, p, fg);
         if (e != cudaSuccess) return e;
-        tc_out_general_kernel<<<(unsigned)ctas, kOutThreads, SMEM_OUT, st>>>(maps, p, fg);
-        e = cudaGetLastError();
+        e = launch(tc_out_general_kernel, (unsigned)ctas, kOutThreads, SMEM_OUT, true, maps, p, fg);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

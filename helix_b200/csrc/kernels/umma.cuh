@@ -104,6 +104,12 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Programmatic dependent launch: wait until the grids this one was launched
+// behind have completed and their memory is visible (returns at once when it
+// was launched normally); allow the grid launched behind this one to start.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Named barrier among `n` threads (id >= 1; id 0 is __syncthreads).
 __device__ __forceinline__ void named_sync(uint32_t id, uint32_t n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
