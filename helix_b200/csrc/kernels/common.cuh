@@ -8,10 +8,32 @@
 
 namespace hx {
 
+// log(1 + e^v) for v <= 20 as max(v, 0) + log1p(u), u = e^-|v| in (0, 1],
+// with log1p(u) = 2 atanh(s) = 2 (s + s^3/3 + s^5/5 + ... + s^15/15),
+// s = u / (2 + u) <= 1/3 (the Taylor series of atanh; the first omitted term
+// is below 2e-9 of the sum).  One exp2 and one fast divide: a few ulp from
+// the correctly rounded value, against two full library calls on the chain
+// of every chunk's decay vectors.
+__device__ __forceinline__ float softplus_le20(float v) {
+    float u;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(u) : "f"(-fabsf(v) * 1.4426950408889634f));
+    const float s = __fdividef(u, 2.0f + u);
+    const float s2 = s * s;
+    float t = 1.0f / 15.0f;
+    t = fmaf(t, s2, 1.0f / 13.0f);
+    t = fmaf(t, s2, 1.0f / 11.0f);
+    t = fmaf(t, s2, 1.0f / 9.0f);
+    t = fmaf(t, s2, 1.0f / 7.0f);
+    t = fmaf(t, s2, 1.0f / 5.0f);
+    t = fmaf(t, s2, 1.0f / 3.0f);
+    t = fmaf(t, s2, 1.0f);
+    return fmaxf(v, 0.0f) + 2.0f * s * t;
+}
+
 // softplus with the v > 20 shortcut, then the clamp
 // (reference src/kernels/helix_common.h:14-20, src/reference/scan_ref.cpp:13-24).
 __device__ __forceinline__ float dt_of(float raw, float lo, float hi) {
-    float v = raw > 20.0f ? raw : log1pf(expf(raw));
+    float v = raw > 20.0f ? raw : softplus_le20(raw);
     v = v < lo ? lo : v;
     v = v > hi ? hi : v;
     return v;

@@ -44,13 +44,22 @@ extern __device__ unsigned long long hx_phase_cycles[32];
 // Timeline of one CTA (blockIdx.x == HX_TL_CTA): clock64 of event `ev` in
 // chunk `i`.
 extern __device__ long long hx_tl[32 * 64];
-extern __device__ unsigned long long hx_cta[512 * 4];
+extern __device__ unsigned long long hx_cta[1024 * 4];
 __device__ __forceinline__ unsigned long long hx_gtime() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
 }
-#define HX_CTA(k) do { if (threadIdx.x == 0 && blockIdx.x < 512) hx_cta[blockIdx.x * 4 + (k)] = hx_gtime(); } while (0)
+#define HX_CTA(k) do { if (threadIdx.x == 0 && blockIdx.x < 1024) hx_cta[blockIdx.x * 4 + (k)] = hx_gtime(); } while (0)
+#define HX_CTA_T(k) do { if (blockIdx.x < 1024) hx_cta[blockIdx.x * 4 + (k)] = hx_gtime(); } while (0)
+// State-kernel timeline of CTAs 40 and 340: globaltimer of event `ev` at
+// step `i`.
+extern __device__ unsigned long long hx_tls[2 * 16 * 64];
+#define HX_TLS(ev, i)                                                                          \
+    do {                                                                                       \
+        if ((blockIdx.x == 40 || blockIdx.x == 340) && (i) < 64)                                \
+            hx_tls[(blockIdx.x == 340) * 1024 + (ev) * 64 + (i)] = hx_gtime();                  \
+    } while (0)
 #define HX_TL_CTA 40
 #define HX_TL(ev, i)                                                          \
     do {                                                                      \
@@ -59,6 +68,8 @@ __device__ __forceinline__ unsigned long long hx_gtime() {
 #else
 #define HX_TL(ev, i) do {} while (0)
 #define HX_CTA(k) do {} while (0)
+#define HX_CTA_T(k) do {} while (0)
+#define HX_TLS(ev, i) do {} while (0)
 #define HX_PHASE_START do {} while (0)
 #define HX_PHASE(k) do {} while (0)
 #define HX_PHASE_T(k, who) do {} while (0)
@@ -1378,7 +1389,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const PairTile pt = pair_tile(p);
-    HX_CTA(0);
     grid_dep_launch();  // the general-path kernel waits for this grid anyway
     if (tid == 0) HX_TL(31, 0);
     if (tid == 0) {
@@ -1454,11 +1464,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (warp == kPWarpMma) tmem_dealloc(tm, 512);
         return;
     }
-    HX_CTA(1);
     out_pair(maps, p, pt, sm, tm, cb_bar, pre);
     tc_fence_before();
     __syncthreads();
-    HX_CTA(2);
     if (warp == kPWarpMma) {
         tc_fence_after();
         tmem_dealloc(tm, 512);
@@ -1577,18 +1585,19 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
 
 // ---------------------------------------------------------------------------
 // State kernel: the run's state from a zero start, G4 accumulated over the
-// whole run in one TMEM accumulator, plus the run's log-decay.  Sized for two
-// CTAs per SM (107 KB of shared memory, 128 TMEM columns, 320 threads): the
-// two CTAs hide each other's latencies.  It streams in 64-token steps (half
-// chunks), which buys three-deep rings for B and x and two xw buffers within
-// that budget, so no load latency sits on the MMA chain.
+// whole run in one TMEM accumulator, plus the run's log-decay.  Sized for
+// three CTAs per SM (69 KB of shared memory, 128 TMEM columns, 320 threads):
+// the CTAs hide each other's latencies.  It streams in 64-token steps (half
+// chunks) through two-deep B and x rings and one xw buffer.
 //
-//   warps 0-7  (256)  xw = w x as bf16 hi | lo from the x ring
-//   warp 8  (lane 0)  TMA producer (B and x, 3 stages each) and MMA issuer:
-//                     per step four 128 x 128 x 16 MMAs, A = B (MN-major),
+//   warps 0-7  (256)  xw = w x as bf16 hi | lo from the x ring, each warp on
+//                     its own waits (no block barrier per step)
+//   warp 8  (lane 0)  TMA producer (B and x) and MMA issuer: per step four
+//                     128 x 128 x 16 MMAs, A = B (MN-major),
 //                     B = [xw_hi | xw_lo] (MN-major)
 //   warp 9            decay weights w_j = dt_j exp(sum_{i>j in run} A dt_i)
-//                     per 128-token chunk into a 4-slot ring
+//                     per 128-token chunk into a 4-slot ring; its dt loads
+//                     run three chunks ahead through a shared-memory ring
 //
 // Chunks are visited last to first so the decay from token j to the end of
 // the run is a sum of same-sign terms.
@@ -1596,27 +1605,36 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
 constexpr int kStEpi = 256;
 constexpr int kStThreads = kStEpi + 64;
 constexpr int kStHalf = 64;                            // tokens per step
-constexpr int kStStages = 3;
+// Two-deep B and x rings and one xw buffer keep a CTA at 69 KB of shared
+// memory, so three CTAs share an SM: more CTAs in flight hide the load
+// latency of each step better than deeper rings in fewer CTAs.
+constexpr int kStB = 2;                                // B ring depth
+constexpr int kStX = 2;                                // x ring depth
+constexpr int kStXw = 1;                               // xw buffers
+constexpr int kStCtas = 3;                             // CTAs per SM
 constexpr int kStRing = 4;
-constexpr uint32_t SO_B = 0;                           // 3 x 16 KB: B rows of one step, states 0-63 | 64-127
-constexpr uint32_t SO_X = SO_B + kStStages * 16384;    // 3 x 8 KB: x rows of one step
-constexpr uint32_t SO_XW = SO_X + kStStages * 8192;    // 2 x (hi 8 KB | lo 8 KB)
-constexpr uint32_t SO_W = SO_XW + 2 * 16384;           // kStRing x 128 weights
-constexpr uint32_t SMEM_STATE = SO_W + kStRing * 512 + 1024;
+constexpr uint32_t SO_B = 0;                           // kStB x 16 KB: B rows of one step, states 0-63 | 64-127
+constexpr uint32_t SO_X = SO_B + kStB * 16384;         // kStX x 8 KB: x rows of one step
+constexpr uint32_t SO_XW = SO_X + kStX * 8192;         // kStXw x (hi 8 KB | lo 8 KB)
+constexpr uint32_t SO_W = SO_XW + kStXw * 16384;       // kStRing x 128 weights
+constexpr uint32_t SO_DT = SO_W + kStRing * 512;         // vector warp's raw dt ring, 4 x 128 floats
+constexpr uint32_t SMEM_STATE = SO_DT + 4 * 512 + 1024;
 
 struct StBars {
-    uint64_t b_full[kStStages], b_done[kStStages], x_full[kStStages], xw_full[2], xw_empty[2];
+    uint64_t b_full[kStB], b_done[kStB], x_full[kStX], xw_full[kStXw], xw_empty[kStXw];
     uint64_t w_full[kStRing], w_empty[kStRing];
 };
 
+// Per-warp bounded wait of the builders: no block barrier, so a warp goes on
+// as soon as its own inputs are there.  A warp whose wait ran out records
+// the fault and leaves its loop; every later wait of the kernel is bounded.
 __device__ __forceinline__ bool st_wait(uint64_t* bar, uint32_t parity, unsigned code) {
-    const bool ok = mbar_wait(bar, parity, kWaitBudget);
-    const bool all = named_and(1, kStEpi, ok);
-    if (!all && threadIdx.x == 0) atomicCAS(&g_tc_fault, 0u, code);
+    const bool all = __all_sync(0xffffffffu, mbar_wait(bar, parity, kWaitBudget));
+    if (!all && (threadIdx.x & 31) == 0) atomicCAS(&g_tc_fault, 0u, code);
     return all;
 }
 
-__global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_constant__ TcMaps maps, ScanParams p,
+__global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __grid_constant__ TcMaps maps, ScanParams p,
                                                                  int runs_in_grid) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
@@ -1626,6 +1644,8 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
     __shared__ float lam_total;
 
     HX_PHASE_START;
+    HX_CTA(0);
+    if (threadIdx.x == 0) HX_TLS(0, 0);
     const int tid = threadIdx.x, warp = tid >> 5;
     const bool is_mma = warp == 8, is_vec = warp == 9;
     const int wg = (warp >> 2) & 1;
@@ -1643,17 +1663,26 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
     const int64_t db = (int64_t)tl.seq * p.seq_dt + (int64_t)tl.h * p.s_dt1;
     auto t0_of = [&](int q) { return t_begin + (n_ch - 1 - q) * kCS; };       // visit order q -> chunk
     auto ts_of = [&](int s) { return t0_of(s >> 1) + (s & 1) * kStHalf; };    // step s -> first token
-    auto sB = [&](int s) { return sm + SO_B + (uint32_t)(s % kStStages) * 16384u; };
-    auto sX = [&](int s) { return sm + SO_X + (uint32_t)(s % kStStages) * 8192u; };
-    auto sXW = [&](int s) { return sm + SO_XW + (uint32_t)(s & 1) * 16384u; };
+    // the decay-weight warp issues the dt loads of its first three chunks
+    // before any set-up, so their latency overlaps it and the first TMA waits
+    float r0[4], r1[4], r2[4];
+    if (is_vec) {
+        warp_load_dt(p, db, t0_of(0), t_end, r0);
+        warp_load_dt(p, db, t0_of(min(1, n_ch - 1)), t_end, r1);
+        warp_load_dt(p, db, t0_of(min(2, n_ch - 1)), t_end, r2);
+        if ((tid & 31) == 0) HX_TLS(15, 0);
+    }
+    auto sB = [&](int s) { return sm + SO_B + (uint32_t)(s % kStB) * 16384u; };
+    auto sX = [&](int s) { return sm + SO_X + (uint32_t)(s % kStX) * 8192u; };
+    auto sXW = [&](int s) { return sm + SO_XW + (uint32_t)(s % kStXw) * 16384u; };
 
     if (tid == 0) {
-        for (int k = 0; k < kStStages; ++k) {
+        for (int k = 0; k < kStB; ++k) {
             mbar_init(&bars.b_full[k], 1);
             mbar_init(&bars.b_done[k], 1);
-            mbar_init(&bars.x_full[k], 1);
         }
-        for (int k = 0; k < 2; ++k) {
+        for (int k = 0; k < kStX; ++k) mbar_init(&bars.x_full[k], 1);
+        for (int k = 0; k < kStXw; ++k) {
             mbar_init(&bars.xw_full[k], kStEpi / 32);
             mbar_init(&bars.xw_empty[k], 1);
         }
@@ -1672,13 +1701,13 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
     const uint32_t tm = tmem_base;
 
     auto load_b = [&](int s) {
-        uint64_t* bar = &bars.b_full[s % kStStages];
+        uint64_t* bar = &bars.b_full[s % kStB];
         mbar_expect_tx(bar, 2 * 8192);
         tma_load_4d(sB(s), &maps.b, bar, 0, g, ts_of(s), tl.seq);
         tma_load_4d(sB(s) + 8192, &maps.b, bar, 64, g, ts_of(s), tl.seq);
     };
     auto load_x = [&](int s) {
-        uint64_t* bar = &bars.x_full[s % kStStages];
+        uint64_t* bar = &bars.x_full[s % kStX];
         mbar_expect_tx(bar, 8192);
         tma_load_4d(sX(s), &maps.x, bar, p0, tl.h, ts_of(s), tl.seq);
     };
@@ -1688,17 +1717,17 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
         if ((tid & 31) == 0) {
             prefetch_tmap(&maps.b);
             prefetch_tmap(&maps.x);
-            for (int s = 0; s < kStStages && s < n_st; ++s) {
-                load_b(s);
-                load_x(s);
-            }
+            for (int s = 0; s < kStB && s < n_st; ++s) load_b(s);
+            for (int s = 0; s < kStX && s < n_st; ++s) load_x(s);
             HX_PHASE_T(16, 256);
             for (int s = 0; s < n_st && ok; ++s) {
-                const int st = s % kStStages;
-                const uint32_t pf = (uint32_t)((s / kStStages) & 1);
-                if (!(ok = mbar_wait(&bars.b_full[st], pf, kWaitBudget))) break;
+                const int st = s % kStB;
+                if (!(ok = mbar_wait(&bars.b_full[st], (uint32_t)((s / kStB) & 1), kWaitBudget))) break;
+                if (s == 0 && blockIdx.x < 1024) HX_CTA_T(1);
+                HX_TLS(1, s);
                 HX_PHASE_T(17, 256);
-                if (!(ok = mbar_wait(&bars.xw_full[s & 1], (uint32_t)((s >> 1) & 1), kWaitBudget))) break;
+                if (!(ok = mbar_wait(&bars.xw_full[s % kStXw], (uint32_t)((s / kStXw) & 1), kWaitBudget))) break;
+                HX_TLS(2, s);
                 HX_PHASE_T(18, 256);
                 tc_fence_after();
                 // A = B rows of the step (M = 128 states in two 64-state atoms),
@@ -1708,15 +1737,18 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks)
                     mma_bf16(tm, desc_add(dA, 2048u * ks), desc_add(dX, 2048u * ks), ID_G4W, (s > 0 || ks > 0) ? 1u : 0u);
-                mma_commit(&bars.xw_empty[s & 1]);
+                mma_commit(&bars.xw_empty[s % kStXw]);
                 mma_commit(&bars.b_done[st]);
+                if (s + 1 == n_st) HX_CTA_T(2);
+                HX_TLS(3, s);
                 HX_PHASE_T(19, 256);
-                if (s + kStStages < n_st) {
-                    // the builders consumed x(s) before xw_full; B(s) is free once
-                    // these MMAs retire
-                    load_x(s + kStStages);
-                    if (!(ok = mbar_wait(&bars.b_done[st], pf, kWaitBudget))) break;
-                    load_b(s + kStStages);
+                // the builders consumed x(s) before xw_full
+                if (s + kStX < n_st) load_x(s + kStX);
+                // B(s)'s slot takes B(s + kStB) once this step's MMAs retire
+                if (s + kStB < n_st) {
+                    if (!(ok = mbar_wait(&bars.b_done[st], (uint32_t)((s / kStB) & 1), kWaitBudget))) break;
+                    load_b(s + kStB);
+                    HX_TLS(4, s);
                 }
                 HX_PHASE_T(20, 256);
             }
@@ -1728,32 +1760,52 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
         __syncwarp();
     } else if (is_vec) {
         // ---- decay weights, ahead of the builders --------------------------
+        // raw dt of chunk q+3 is loaded while chunk q is processed and parked
+        // in a private shared-memory ring, so no chunk waits a load round trip
         const float Ah2 = Ah * kLog2e;
+        const int lane = tid & 31;
+        float* dtr = reinterpret_cast<float*>(sm + SO_DT);
         float later = 0.0f;  // log2 units: sum of A*dt over chunks after this one
-        float raw[4], raw_next[4];
-        warp_load_dt(p, db, t0_of(0), t_end, raw);
+        auto park = [&](int q, const float (&r)[4]) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dtr[(q & 3) * 128 + 4 * lane + k] = r[k];
+        };
+        park(0, r0);
+        __syncwarp();
+        if (lane == 0) HX_TLS(10, 0);
+#pragma unroll 1
         for (int q = 0; q < n_ch && ok; ++q) {
             const int t0 = t0_of(q);
-            if (q + 1 < n_ch) warp_load_dt(p, db, t0_of(q + 1), t_end, raw_next);
+            float nx[4];
+            const bool more = q + 3 < n_ch;
+            if (more) warp_load_dt(p, db, t0_of(q + 3), t_end, nx);
+            const float raw[4] = {dtr[(q & 3) * 128 + 4 * lane], dtr[(q & 3) * 128 + 4 * lane + 1],
+                                  dtr[(q & 3) * 128 + 4 * lane + 2], dtr[(q & 3) * 128 + 4 * lane + 3]};
             float v[4], pre[4], total;
+            if (lane == 0) HX_TLS(13, q);
             warp_chunk_prefix(p, db, t0, min(kCS, t_end - t0), Ah2, raw, v, pre, &total);
+            if (lane == 0) HX_TLS(14, q);
             const int slot = q % kStRing;
             if (q >= kStRing) {
                 if (!(ok = mbar_wait(&bars.w_empty[slot], (uint32_t)(((q - kStRing) / kStRing) & 1), kWaitBudget)))
                     break;
             }
             float* w = wring + slot * 128;
-            const int lane = tid & 31;
 #pragma unroll
             for (int k = 0; k < 4; ++k) w[4 * lane + k] = v[k] * ex2(later + (total - pre[k]));
             later += total;
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars.w_full[slot]);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) raw[k] = raw_next[k];
+            if (lane == 0) HX_TLS(9, q);
+            if (q == 0) {
+                park(1, r1);
+                park(2, r2);
+            }
+            if (more) park(q + 3, nx);
+            __syncwarp();
         }
         if (!ok) atomicCAS(&g_tc_fault, 0u, kFaultMmaState);
-        if ((tid & 31) == 0) lam_total = later / kLog2e;
+        if (lane == 0) lam_total = later / kLog2e;
         __syncwarp();
     } else {
         // ---- xw builders: two 16-byte x vectors per thread per step -------
@@ -1763,11 +1815,15 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
             if ((s & 1) == 0) {
                 if (!(ok = st_wait(&bars.w_full[slot], (uint32_t)((q / kStRing) & 1), kFaultMmaState))) break;
             }
+            if (tid == 0) HX_TLS(5, s);
             HX_PHASE(22);
-            if (!(ok = st_wait(&bars.x_full[s % kStStages], (uint32_t)((s / kStStages) & 1), kFaultTmaState))) break;
-            if (s >= 2) {  // xw buffer s & 1 was last read by step s - 2
-                if (!(ok = st_wait(&bars.xw_empty[s & 1], (uint32_t)(((s - 2) >> 1) & 1), kFaultMmaState))) break;
+            if (!(ok = st_wait(&bars.x_full[s % kStX], (uint32_t)((s / kStX) & 1), kFaultTmaState))) break;
+            if (tid == 0) HX_TLS(6, s);
+            if (s >= kStXw) {  // xw buffer s % kStXw was last read by step s - kStXw
+                if (!(ok = st_wait(&bars.xw_empty[s % kStXw], (uint32_t)(((s - kStXw) / kStXw) & 1), kFaultMmaState)))
+                    break;
             }
+            if (tid == 0) HX_TLS(7, s);
             HX_PHASE(23);
             const float* wv = wring + slot * 128 + (s & 1) * kStHalf;
             const uint8_t* x = sX(s);
@@ -1798,14 +1854,16 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
             fence_async_smem();
             __syncwarp();
             if ((tid & 31) == 0) {
-                mbar_arrive(&bars.xw_full[s & 1]);
+                mbar_arrive(&bars.xw_full[s % kStXw]);
                 if (s & 1) mbar_arrive(&bars.w_empty[slot]);
             }
+            if (tid == 0) HX_TLS(8, s);
             HX_PHASE(25);
         }
         // all G4 MMAs retired: the last step's commit
         if (ok && n_st > 0)
-            ok = st_wait(&bars.xw_empty[(n_st - 1) & 1], (uint32_t)(((n_st - 1) >> 1) & 1), kFaultMmaState);
+            ok = st_wait(&bars.xw_empty[(n_st - 1) % kStXw], (uint32_t)(((n_st - 1) / kStXw) & 1), kFaultMmaState);
+        if (tid == 0) HX_TLS(11, 0);
         tc_fence_after();
         if (ok) {
             const int64_t unit = ((int64_t)tl.seq * p.H + tl.h) * p.run_slots + tl.run;
@@ -1829,6 +1887,8 @@ __global__ void __launch_bounds__(kStThreads, 2) tc_state_kernel(const __grid_co
     __syncthreads();
     if (ok && tid == 0 && tl.slab == 0)
         p.lam[((int64_t)tl.seq * p.H + tl.h) * p.run_slots + tl.run] = lam_total;
+    HX_CTA(3);
+    if (tid == 0) HX_TLS(12, 0);
     if (is_mma) {
         tc_fence_after();
         tmem_dealloc(tm, 128);

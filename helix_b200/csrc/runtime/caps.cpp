@@ -124,19 +124,23 @@ void tc_split(const helix_scan_desc& d, int blocks, int n_sm, int max_runs, int*
     const int n_out = (blocks + sb - 1) / sb;
     int k = 1;
     if (n_out > 1) {
+        // Runs per span for the state kernel: each CTA reduces one run of one
+        // slab, kStateCtasPerSm CTAs share an SM, and a CTA costs about
+        // kStateStartSteps 64-token steps of set-up on top of two steps per
+        // 128-token block.  Pick the divisor of the span that minimises
+        // waves x per-CTA steps, within the run-slot budget.
         const int64_t st_units = (int64_t)d.n_seq * d.n_head * ((d.head_dim + kSlab - 1) / kSlab) * (n_out - 1);
-        const int64_t want = std::max<int64_t>(1, (4 * (int64_t)n_sm + st_units - 1) / st_units);
-        k = sb;
-        for (int c = 1; c <= sb; ++c)
-            if (sb % c == 0 && c >= want) {
+        const int64_t slots = (int64_t)kStateCtasPerSm * n_sm;
+        double kbest = 1e300;
+        for (int c = 1; c <= sb; ++c) {
+            if (sb % c != 0) continue;
+            if ((int64_t)(blocks + sb / c - 1) / (sb / c) > max_runs) break;
+            const int64_t waves = (st_units * c + slots - 1) / slots;
+            const double cost = (double)waves * (kStateStartSteps + 2.0 * (sb / c));
+            if (cost < kbest) {
+                kbest = cost;
                 k = c;
-                break;
             }
-        // stay within the run-slot budget
-        while (k > 1 && (int64_t)(blocks + sb / k - 1) / (sb / k) > max_runs) {
-            int c = k - 1;
-            while (c > 1 && sb % c != 0) --c;
-            k = c;
         }
     }
     *run_blocks = sb / k;

@@ -31,6 +31,10 @@ constexpr int kSlab = 64;
 // Upper bound on runs per sequence (the output kernels stage per-run decays
 // and carry weights in shared memory).
 constexpr int kMaxRuns = 256;
+// Tensor-core state kernel: CTAs resident per SM, and its fixed cost per CTA
+// (first loads, first decay weights, drain) in 64-token steps, as measured.
+constexpr int kStateCtasPerSm = 3;
+constexpr double kStateStartSteps = 3.5;
 
 enum Path : int {
     kPathSimtF32 = 0,   // exact fp32 CUDA-core kernels
