@@ -500,23 +500,11 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                 const int idx = r + kGXwThreads * k;
                 const int j = idx >> 3, c = idx & 7;
                 const uint32_t off = sw128_off(j, c);
-                const uint4 rw = *reinterpret_cast<const uint4*>(x + off);
                 const float wj = wv[j];
-                const uint32_t in[4] = {rw.x, rw.y, rw.z, rw.w};
-                uint32_t hi[4], lo[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    float a, b;
-                    unpack_bf16x2(in[e], a, b);
-                    a *= wj;
-                    b *= wj;
-                    hi[e] = pack_bf16x2(a, b);
-                    float ah, bh;
-                    unpack_bf16x2(hi[e], ah, bh);
-                    lo[e] = pack_bf16x2(a - ah, b - bh);
-                }
-                *reinterpret_cast<uint4*>(sXW + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(sXW + 16384 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                uint4 hi, lo;
+                split_xw8(*reinterpret_cast<const uint4*>(x + off), f2_of(wj, wj), hi, lo);
+                *reinterpret_cast<uint4*>(sXW + off) = hi;
+                *reinterpret_cast<uint4*>(sXW + 16384 + off) = lo;
             }
             fence_async_smem();
             __syncwarp();
@@ -800,10 +788,9 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
 // with j0 = r >> 4, sl = (r >> 3) & 1 and c = r & 7 the same for every k
 // (kPBldThreads is a multiple of 16), so one row pointer per thread serves all
 // its vectors.  The fast path runs only when P is a multiple of 8, so every
-// vector lies inside or outside its slab as a whole.  Vectors are loaded
-// without a condition on their value (ones that do not exist read the
-// tensor's first vector and are zeroed where they are used), so nothing waits
-// for the loads before their use.
+// vector lies inside or outside its slab as a whole.  Vectors that do not
+// exist read sixteen zero bytes instead, so they need no test where they are
+// used.
 constexpr int kJStep = kPBldThreads / 16;
 static_assert(kPBldThreads % 16 == 0, "builder vectors keep their slab and channels");
 struct XLane {
@@ -822,18 +809,21 @@ __device__ __forceinline__ XLane x_lane(const ScanParams& p, const PairTile& pt,
              8 * xl.c;
     return xl;
 }
-__device__ __forceinline__ bool x_ok(const XLane& xl, const PairTile& pt, int i, int k) {
-    const int j = xl.j0 + kJStep * k;
-    return xl.c_in && j < kCS && pt.t_begin + i * kCS + j < pt.t_end;
-}
+// Sixteen zero bytes: the source of every x vector outside the tensor, so a
+// vector needs no test where it is used.
+__device__ uint4 g_x_zero;
 __device__ __forceinline__ void load_x_pair(const ScanParams& p, const PairTile& pt, const XLane& xl, int i,
                                             uint4 (&v)[kPV]) {
-    const __nv_bfloat16* xg = static_cast<const __nv_bfloat16*>(p.x);
-    const __nv_bfloat16* base = xl.row + (int64_t)(pt.t_begin + i * kCS + xl.j0) * p.s_x0;
-    const int64_t step = (int64_t)kJStep * p.s_x0;
+    const int t0 = pt.t_begin + i * kCS + xl.j0;  // this thread's first row
+    const int rem = xl.c_in ? pt.t_end - t0 : 0;    // rows of it left in the tensor
+    const char* src = reinterpret_cast<const char*>(xl.row + (int64_t)t0 * p.s_x0);
+    const int64_t step = (int64_t)kJStep * p.s_x0 * (int64_t)sizeof(__nv_bfloat16);
 #pragma unroll
-    for (int k = 0; k < kPV; ++k)
-        v[k] = __ldg(reinterpret_cast<const uint4*>(x_ok(xl, pt, i, k) ? base + k * step : xg));
+    for (int k = 0; k < kPV; ++k) {
+        const bool in = kJStep * k < rem && (k < kPV - 1 || xl.j0 + kJStep * k < kCS);
+        v[k] = __ldg(in ? reinterpret_cast<const uint4*>(src) : &g_x_zero);
+        src += step;
+    }
 }
 
 // State tile of a pair in shared memory: row r = 64 v + c (slab v, channel
@@ -1105,29 +1095,19 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             // reads the span-entry state staged over these buffers
             if (!(ok = i >= 1 ? warp_wait(&bars.g4, (uint32_t)((i - 1) & 1)) : warp_wait(&bars.s_ready, 0u))) break;
             if (lead) HX_TL(17, i);
+            // rows of this thread's vectors: j0 + 12 k; the swizzled 16-byte
+            // column depends on the row only through bit 2 (k odd flips it)
             const float* wv = slot(i) + kPSlot * xl.sl + xl.j0;
+            uint8_t* lo_e = xt + 32768u + sw128_off(xl.j0, xl.c);
+            uint8_t* lo_o = xt + 32768u + sw128_off(xl.j0 + kJStep, xl.c) - 128u * kJStep;
 #pragma unroll
             for (int k = 0; k < kPV; ++k) {
-                const int j = xl.j0 + kJStep * k;
-                if (j < kCS) {
+                if (k < kPV - 1 || xl.j0 + kJStep * k < kCS) {
                     const float wj = wv[kJStep * k];
-                    const bool xv = x_ok(xl, pt, i, k);
-                    const uint32_t in[4] = {xv ? cur[k].x : 0u, xv ? cur[k].y : 0u, xv ? cur[k].z : 0u,
-                                            xv ? cur[k].w : 0u};
-                    uint32_t hi[4], lo[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        float a, b;
-                        unpack_bf16x2(in[e], a, b);
-                        a *= wj;
-                        b *= wj;
-                        hi[e] = pack_bf16x2(a, b);
-                        float ah, bh;
-                        unpack_bf16x2(hi[e], ah, bh);
-                        lo[e] = pack_bf16x2(a - ah, b - bh);
-                    }
-                    *reinterpret_cast<uint4*>(xt + 32768u + sw128_off(j, xl.c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                    cur[k] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    uint4 hi, lo;
+                    split_xw8(cur[k], f2_of(wj, wj), hi, lo);
+                    *reinterpret_cast<uint4*>((k & 1 ? lo_o : lo_e) + 128u * kJStep * k) = lo;
+                    cur[k] = hi;
                 }
             }
             if (lead) HX_TL(18, i);
@@ -1135,10 +1115,9 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             if (i >= 1 && !(ok = warp_wait(&bars.g2, (uint32_t)((i - 1) & 1)))) break;
             if (lead) HX_TL(19, i);
 #pragma unroll
-            for (int k = 0; k < kPV; ++k) {
-                const int j = xl.j0 + kJStep * k;
-                if (j < kCS) *reinterpret_cast<uint4*>(xt + sw128_off(j, xl.c)) = cur[k];
-            }
+            for (int k = 0; k < kPV; ++k)
+                if (k < kPV - 1 || xl.j0 + kJStep * k < kCS)
+                    *reinterpret_cast<uint4*>((k & 1 ? lo_o : lo_e) - 32768u + 128u * kJStep * k) = cur[k];
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -1276,9 +1255,9 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 tc_fence_before();
                 warp_arrive(&bars.y_free);
                 if (tid == 0) HX_TL(14, i);
-                // one 128-byte row (32 channels) per store
                 const float4* f4 = reinterpret_cast<const float4*>(slot(i) + kPSlot * v + 128 + 64 * kh);
                 if (c_ok) {
+                    // one 128-byte row (32 channels) per store
                     float* yp = p.y + (int64_t)pt.seq * p.seq_y + (int64_t)(tp + 64 * kh) * p.s_y0 +
                                 (int64_t)sr.h * p.s_y1 + (int64_t)(sr.p0 + c) * p.s_y2;
                     const int64_t sy = p.s_y0;
@@ -1834,22 +1813,10 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
                 const int j = i >> 3, c = i & 7;
                 const uint32_t off = sw128_off(j, c);
                 const float wj = wv[j];
-                const uint4 xr = *reinterpret_cast<const uint4*>(x + off);
-                const uint32_t in[4] = {xr.x, xr.y, xr.z, xr.w};
-                uint32_t hi[4], lo[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    float a, b;
-                    unpack_bf16x2(in[e], a, b);
-                    a *= wj;
-                    b *= wj;
-                    hi[e] = pack_bf16x2(a, b);
-                    float ah, bh;
-                    unpack_bf16x2(hi[e], ah, bh);
-                    lo[e] = pack_bf16x2(a - ah, b - bh);
-                }
-                *reinterpret_cast<uint4*>(xh + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(xh + 8192 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                uint4 hi, lo;
+                split_xw8(*reinterpret_cast<const uint4*>(x + off), f2_of(wj, wj), hi, lo);
+                *reinterpret_cast<uint4*>(xh + off) = hi;
+                *reinterpret_cast<uint4*>(xh + 8192 + off) = lo;
             }
             fence_async_smem();
             __syncwarp();

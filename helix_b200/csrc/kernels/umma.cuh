@@ -280,5 +280,49 @@ __device__ __forceinline__ void unpack_bf16x2(uint32_t w, float& lo, float& hi) 
     hi = f.y;
 }
 
+// Two fp32 lanes in one 64-bit register pair: sm_100 multiplies or subtracts
+// both with one instruction (mul/sub .f32x2).
+__device__ __forceinline__ uint64_t f2_of(float lo, float hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ void f2_to(uint64_t d, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(d));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// bf16 pair -> fp32 pair (exact: a bf16 is the top half of its fp32)
+__device__ __forceinline__ uint64_t f2_of_bf16x2(uint32_t w) {
+    return f2_of(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+// x w for 8 bf16 x and one fp32 w, as bf16 hi = round(x w) and
+// lo = round(x w - hi): hi + lo carries x w to about 16 significant bits.
+__device__ __forceinline__ void split_xw8(const uint4& x, uint64_t w2, uint4& hi, uint4& lo) {
+    const uint32_t in[4] = {x.x, x.y, x.z, x.w};
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const uint64_t p = f2_mul(f2_of_bf16x2(in[e]), w2);
+        float p0, p1;
+        f2_to(p, p0, p1);
+        h[e] = pack_bf16x2(p0, p1);
+        float l0, l1;
+        f2_to(f2_sub(p, f2_of_bf16x2(h[e])), l0, l1);
+        l[e] = pack_bf16x2(l0, l1);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 }  // namespace umma
 }  // namespace hx
