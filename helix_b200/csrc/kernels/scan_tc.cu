@@ -60,6 +60,15 @@ extern __device__ unsigned long long hx_tls[2 * 16 * 64];
         if ((blockIdx.x == 40 || blockIdx.x == 340) && (i) < 64)                                \
             hx_tls[(blockIdx.x == 340) * 1024 + (ev) * 64 + (i)] = hx_gtime();                  \
     } while (0)
+// Grid-wide spans: earliest event `k` (slot 2k) and latest (slot 2k+1) over
+// the CTAs that reach it.
+extern __device__ unsigned long long hx_kspan[32];
+#define HX_KS(k)                                                  \
+    do {                                                          \
+        const unsigned long long t_ = hx_gtime();                 \
+        atomicMin(&hx_kspan[2 * (k)], t_);                        \
+        atomicMax(&hx_kspan[2 * (k) + 1], t_);                    \
+    } while (0)
 #define HX_TL_CTA 40
 #define HX_TL(ev, i)                                                          \
     do {                                                                      \
@@ -70,6 +79,7 @@ extern __device__ unsigned long long hx_tls[2 * 16 * 64];
 #define HX_CTA(k) do {} while (0)
 #define HX_CTA_T(k) do {} while (0)
 #define HX_TLS(ev, i) do {} while (0)
+#define HX_KS(k) do {} while (0)
 #define HX_PHASE_START do {} while (0)
 #define HX_PHASE(k) do {} while (0)
 #define HX_PHASE_T(k, who) do {} while (0)
@@ -1127,6 +1137,12 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             if (lead) HX_TL(20, i);
 #pragma unroll
             for (int k = 0; k < kPV; ++k) cur[k] = nxt[k];
+#ifdef HX_PHASE_PROFILE
+            if (lead) {
+                asm volatile("" ::"r"(cur[0].x), "r"(cur[kPV - 2].w));
+                HX_TL(28, i);
+            }
+#endif
         }
     } else {
         // ================= epilogue =========================================
@@ -1149,10 +1165,16 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                     tmem_ld16(tm + lo + TP_D1 + col + 32 * h2, *reinterpret_cast<float(*)[16]>(d));
                     tmem_ld16(tm + lo + TP_D1 + col + 32 * h2 + 16, *reinterpret_cast<float(*)[16]>(d + 16));
                     tmem_wait_ld();
+                    if (j0 == 32 * q) {  // the diagonal block: keep j <= t
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int j = j0 + 2 * e;
-                        mk[16 * h2 + e] = pack_bf16x2(j <= lane_row ? d[2 * e] : 0.0f, j + 1 <= lane_row ? d[2 * e + 1] : 0.0f);
+                        for (int e = 0; e < 16; ++e) {
+                            const int j = j0 + 2 * e;
+                            mk[16 * h2 + e] =
+                                pack_bf16x2(j <= lane_row ? d[2 * e] : 0.0f, j + 1 <= lane_row ? d[2 * e + 1] : 0.0f);
+                        }
+                    } else {  // wholly below the diagonal (j0 < 32 q for the whole warp)
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) mk[16 * h2 + e] = pack_bf16x2(d[2 * e], d[2 * e + 1]);
                     }
                 } else {
 #pragma unroll
@@ -1165,16 +1187,18 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
         // S~ = decay S -> D4 (fp32) and its bf16 pairs -> S~ columns, for the
         // 32 state columns 32 h2 .. +31 of this thread's half
         auto put_state32 = [&](float (&s)[32], int h2, float decay) {
+            const uint64_t dd = f2_of(decay, decay);
 #pragma unroll
             for (int g = 0; g < 2; ++g) {
                 uint32_t f[16], b[8];
 #pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                    s[16 * g + k] *= decay;
-                    f[k] = __float_as_uint(s[16 * g + k]);
+                for (int k = 0; k < 8; ++k) {
+                    float u, w;
+                    f2_to(f2_mul(f2_of(s[16 * g + 2 * k], s[16 * g + 2 * k + 1]), dd), u, w);
+                    f[2 * k] = __float_as_uint(u);
+                    f[2 * k + 1] = __float_as_uint(w);
+                    b[k] = pack_bf16x2(u, w);
                 }
-#pragma unroll
-                for (int k = 0; k < 8; ++k) b[k] = pack_bf16x2(s[16 * g + 2 * k], s[16 * g + 2 * k + 1]);
                 tmem_st16(tm + lo + TP_D4 + col + 32 * h2 + 16 * g, f);
                 tmem_st8(tm + lo + TP_S + 32 * kh + 16 * h2 + 8 * g, b);
             }
@@ -1256,12 +1280,12 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 warp_arrive(&bars.y_free);
                 if (tid == 0) HX_TL(14, i);
                 const float4* f4 = reinterpret_cast<const float4*>(slot(i) + kPSlot * v + 128 + 64 * kh);
+                const int kmax = tlen - 64 * kh;
                 if (c_ok) {
                     // one 128-byte row (32 channels) per store
                     float* yp = p.y + (int64_t)pt.seq * p.seq_y + (int64_t)(tp + 64 * kh) * p.s_y0 +
                                 (int64_t)sr.h * p.s_y1 + (int64_t)(sr.p0 + c) * p.s_y2;
                     const int64_t sy = p.s_y0;
-                    const int kmax = tlen - 64 * kh;
 #pragma unroll
                     for (int k4 = 0; k4 < 16; ++k4) {
                         const float4 fv = f4[k4];
@@ -1370,6 +1394,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const PairTile pt = pair_tile(p);
     grid_dep_launch();  // the general-path kernel waits for this grid anyway
     if (tid == 0) HX_TL(31, 0);
+    if (tid == 0) HX_KS(5);
     if (tid == 0) {
         mbar_init(&cb_bar[0], 1);
         mbar_init(&cb_bar[1], 1);
@@ -1396,6 +1421,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // early: everything above reads only the scan's inputs; the carry
         // kernel's span-entry states are read after the wait
         grid_dep_wait();
+        if (tid == 0) HX_KS(6);
         load_state_tile(p, pt, st, tid);
         if (tid == 0) HX_TL(24, 0);
         pair_span(p, pt, warp, kPEpi + kPBld, &span_bits);
@@ -1432,6 +1458,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     __syncthreads();
     if (tid == 0) HX_TL(31, 1);
+    if (tid == 0) HX_KS(7);
     const uint32_t tm = tmem_base;
     const bool fast = pair_takes_fast(p, span_bits, force_general);
     if (tid == 0 && p.tile_flag) p.tile_flag[blockIdx.x] = fast ? 1 : 0;
@@ -1446,6 +1473,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     out_pair(maps, p, pt, sm, tm, cb_bar, pre);
     tc_fence_before();
     __syncthreads();
+    if (tid == 0) HX_KS(8);
     if (warp == kPWarpMma) {
         tc_fence_after();
         tmem_dealloc(tm, 512);
@@ -1518,7 +1546,9 @@ __global__ void __launch_bounds__(kOutThreads, 1)
 constexpr int kCarryThreads = 256;
 
 __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
+    if (threadIdx.x == 0) HX_KS(2);
     grid_dep_wait();    // the state kernel's run states
+    if (threadIdx.x == 0) HX_KS(3);
     grid_dep_launch();  // the output kernel may start its prologue
     const int64_t per_head4 = (int64_t)p.P * p.N / 4;
     const int64_t gid = (int64_t)blockIdx.x * kCarryThreads + threadIdx.x;
@@ -1625,6 +1655,7 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
     HX_PHASE_START;
     HX_CTA(0);
     if (threadIdx.x == 0) HX_TLS(0, 0);
+    if (threadIdx.x == 0) HX_KS(0);
     const int tid = threadIdx.x, warp = tid >> 5;
     const bool is_mma = warp == 8, is_vec = warp == 9;
     const int wg = (warp >> 2) & 1;
@@ -1856,6 +1887,7 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
         p.lam[((int64_t)tl.seq * p.H + tl.h) * p.run_slots + tl.run] = lam_total;
     HX_CTA(3);
     if (tid == 0) HX_TLS(12, 0);
+    if (tid == 0) HX_KS(1);
     if (is_mma) {
         tc_fence_after();
         tmem_dealloc(tm, 128);

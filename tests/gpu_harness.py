@@ -28,15 +28,20 @@ def record(tag: str, **kv):
 
 
 def run(ctx, prob: dict, *, multipass=True, backend=abi.HELIX_BACKEND_AUTO, compute="auto",
-        io="f32", ids=None, desc_hook=None, stream=None, device="cuda:0"):
-    """prob: numpy float32 arrays s0, x, dt, A, B, C in dense helix.h layouts."""
+        io="f32", ids=None, desc_hook=None, stream=None, device="cuda:0", y_view=None):
+    """prob: numpy float32 arrays s0, x, dt, A, B, C in dense helix.h layouts.
+    y_view(shape, device), if given, returns the (possibly strided) y tensor
+    the scan writes."""
     import torch
     dev = torch.device(device)
     io_t = torch.bfloat16 if io == "bf16" else torch.float32
     t = {k: torch.from_numpy(np.ascontiguousarray(prob[k])).to(dev) for k in ("s0", "x", "dt", "A", "B", "C")}
     for k in ("x", "B", "C"):
         t[k] = t[k].to(io_t)
-    y = torch.full(t["x"].shape, float("nan"), dtype=torch.float32, device=dev)
+    if y_view is None:
+        y = torch.full(t["x"].shape, float("nan"), dtype=torch.float32, device=dev)
+    else:
+        y = y_view(t["x"].shape, dev)
     s1 = torch.full(t["s0"].shape, float("nan"), dtype=torch.float32, device=dev)
     d = helix_b200.desc_from_tensors(t["x"], t["dt"], t["B"], t["s0"], y, multipass=multipass,
                                      compute=compute, backend=backend)

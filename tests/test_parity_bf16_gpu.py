@@ -109,6 +109,32 @@ def test_ids_and_batched_bf16(ctx, oracle, run_tokens):
     check_bf16("bf16 ids", y, s1, y_ref, s_ref)
 
 
+def _y_padded_head(shape, dev):
+    """y inside a buffer whose head rows are P + 1 floats apart."""
+    import torch
+    S, L, H, P = shape
+    return torch.full((S, L, H, P + 1), float("nan"), dtype=torch.float32, device=dev)[..., :P]
+
+
+def _y_offset(shape, dev):
+    """Dense y starting 4 bytes past a 16-byte boundary."""
+    import torch
+    n = int(np.prod(shape))
+    return torch.full((n + 1,), float("nan"), dtype=torch.float32, device=dev)[1:].view(shape)
+
+
+@pytest.mark.parametrize("y_view", [_y_padded_head, _y_offset], ids=["padded_head", "offset"])
+def test_strided_y_bf16(ctx, oracle, y_view):
+    """y written through a view: a head stride that is not a multiple of
+    four floats, and a base 4 bytes past a 16-byte boundary."""
+    shape = (300, 2, 4, 64, 128, 2)
+    prob = widen(oracle.harness_problem(*shape, 99, True), "bf16")
+    y_ref, s_ref = _oracle(oracle, prob, shape)
+    y, s1, d = run(ctx, prob, multipass=True, io="bf16", compute="bf16", y_view=y_view)
+    assert "tcgen05" in ctx.backend_desc(d)
+    check_bf16(f"bf16 strided y {y_view.__name__}", y, s1, y_ref, s_ref)
+
+
 def test_c3_full_size_bf16(ctx, oracle):
     """BASELINE config 3 at full size on the BASELINE distributions."""
     from helix_b200.synth import Shape, make_inputs, to_numpy_f32
