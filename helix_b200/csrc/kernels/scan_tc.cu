@@ -102,6 +102,8 @@ enum : unsigned { kFaultTmaOut = 1, kFaultMmaOut = 2, kFaultTmaState = 3, kFault
 
 struct TcMaps {
     CUtensorMap x, b, c;
+    CUtensorMap y;  // fp32 y in 32-channel x 64-token boxes (fast output path)
+    int y_ok;       // y could be described by a tensor map
 };
 
 // TMEM columns.
@@ -781,7 +783,7 @@ constexpr int kPMmaTid = 32 * kPWarpMma;
 __device__ __forceinline__ int bld_index(int warp) { return warp < 10 ? warp - 8 : warp < 14 ? warp - 9 : warp - 10; }
 
 struct PairBars {
-    uint64_t s_ready, y_free, m_ready, d1_free, xw_ready, s1_ready;
+    uint64_t s_ready, y_free, m_ready, d1_free, xw_ready, s1_ready, ys_free;
     uint64_t g3, g4, g2, fin;
     uint64_t v_full[kPRing], v_empty[kPRing];
 };
@@ -939,6 +941,7 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
         mbar_init(&bars.d1_free, kPEpi);
         mbar_init(&bars.xw_ready, kPBld);
         mbar_init(&bars.s1_ready, kPEpi);
+        mbar_init(&bars.ys_free, kPEpi);
         mbar_init(&bars.g3, 1);
         mbar_init(&bars.g4, 1);
         mbar_init(&bars.g2, 1);
@@ -990,6 +993,15 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                     mma_bf16_ts(tm + TP_Y, tm + TP_S + 8u * (uint32_t)ks, desc_add(dC, kmajor_off(ks)), ID_P_KK, ks > 0);
                 mma_commit(&bars.g3);
                 HX_TL(2, i);
+                if (i >= 1 && i + 1 < n_ch) {
+                    // chunk i+1's C/B into chunk i-1's stage once y(i-1),
+                    // staged there after G2(i-1), has left it
+                    if (!(ok = mbar_wait(&bars.ys_free, (uint32_t)((i - 1) & 1), kWaitBudget))) break;
+                    HX_TL(8, i);
+                    load_cb_chunk(maps, sm + OO_CB + 65536u * (uint32_t)((i + 1) & 1), &cb_bar[(i + 1) & 1], pt.g,
+                                  t_begin + (i + 1) * kCS, pt.seq);
+                    cb_issued = i + 2;
+                }
                 if (!(ok = mbar_wait(&bars.xw_ready, par, kWaitBudget))) break;
                 HX_TL(3, i);
                 tc_fence_after();
@@ -1011,14 +1023,6 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 HX_TL(6, i);
                 if (i + 1 < n_ch && !(ok = issue_g1(i + 1))) break;
                 HX_TL(7, i);
-                if (i + 2 < n_ch) {
-                    // G2(i) was the last reader of chunk i's stage (mask over C, B)
-                    if (!(ok = mbar_wait(&bars.g2, par, kWaitBudget))) break;
-                    HX_TL(8, i);
-                    load_cb_chunk(maps, sm + OO_CB + 65536u * (uint32_t)(i & 1), &cb_bar[i & 1], pt.g,
-                                  t_begin + (i + 2) * kCS, pt.seq);
-                    cb_issued = i + 3;
-                }
             }
             if (!ok) atomicCAS(&g_tc_fault, 0u, kFaultMmaOut);
             cb_landed = landed;
@@ -1229,6 +1233,10 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             const uint32_t par = (uint32_t)(i & 1);
             const int tp = t_begin + i * kCS;
             const int tlen = t_end - tp;
+            if (i >= 1) {  // y(i-1) has been read out of its staging buffer
+                if (lane == 0) bulk_wait_read0();
+                warp_arrive(&bars.ys_free);
+            }
             // (1) the mask of D1(i), written over C(i) once G3(i) (and G1(i)
             // before it) retired
             if (!(ok = warp_wait(&bars.g3, par))) break;
@@ -1281,7 +1289,32 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 if (tid == 0) HX_TL(14, i);
                 const float4* f4 = reinterpret_cast<const float4*>(slot(i) + kPSlot * v + 128 + 64 * kh);
                 const int kmax = tlen - 64 * kh;
-                if (c_ok) {
+                if (maps.y_ok && (tlen >= kCS || t_end == p.L)) {
+                    // y through chunk i's C/B stage (free since G2(i)): this
+                    // warp's 64 tokens x 32 channels, 128-byte token rows,
+                    // then one TMA store (rows past L are not written); the
+                    // stage is released at the next chunk
+                    float* yb = reinterpret_cast<float*>(sm + OO_CB + 65536u * (uint32_t)(i & 1) + 8192u * (uint32_t)warp);
+#pragma unroll
+                    for (int k4 = 0; k4 < 16; ++k4) {
+                        const float4 fv = f4[k4];
+                        float y0, y1, y2, y3;
+                        f2_to(f2_mul(f2_of(fv.x, fv.y), f2_of(a[4 * k4], a[4 * k4 + 1])), y0, y1);
+                        f2_to(f2_mul(f2_of(fv.z, fv.w), f2_of(a[4 * k4 + 2], a[4 * k4 + 3])), y2, y3);
+                        yb[(4 * k4) * 32 + lane] = y0;
+                        yb[(4 * k4 + 1) * 32 + lane] = y1;
+                        yb[(4 * k4 + 2) * 32 + lane] = y2;
+                        yb[(4 * k4 + 3) * 32 + lane] = y3;
+                    }
+                    if (tid == 0) HX_TL(22, i);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (tid == 0) HX_TL(23, i);
+                    if (lane == 0 && sr.pw > 32 * (q & 1)) {
+                        tma_store_4d(&maps.y, yb, sr.p0 + 32 * (q & 1), sr.h, tp + 64 * kh, pt.seq);
+                        bulk_commit();
+                    }
+                } else if (c_ok) {
                     // one 128-byte row (32 channels) per store
                     float* yp = p.y + (int64_t)pt.seq * p.seq_y + (int64_t)(tp + 64 * kh) * p.s_y0 +
                                 (int64_t)sr.h * p.s_y1 + (int64_t)(sr.p0 + c) * p.s_y2;
@@ -1300,9 +1333,10 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars.v_empty[i % kPRing]);
                 if (tid == 0) HX_TL(15, i);
-                if (lane == 0 && warp < 2) HX_TL(22 + warp, i);
             }
         }
+        // every y box written before the CTA ends
+        if (lane == 0) bulk_wait0();
         if (ok && pt.last && n_ch > 0) {
             // s1 = D4 after the last G4, through the xw buffers (every MMA has
             // retired: this warp saw the last G2 complete)
@@ -1915,10 +1949,27 @@ bool make_map(EncodeFn fn, CUtensorMap* m, const void* base, int64_t inner, int6
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// fp32 y (chan, head, tok, seq) in 32 x 1 x 64 x 1 boxes, no swizzle: the
+// fast output kernel's TMA stores.  When the channel stride is not 1, or a
+// stride or the base is not 16-byte aligned, there is no map and the kernel
+// stores y with plain stores.
+bool make_y_map(EncodeFn fn, CUtensorMap* m, const ScanParams& p) {
+    if (p.s_y2 != 1) return false;
+    cuuint64_t dims[4] = {(cuuint64_t)p.P, (cuuint64_t)p.H, (cuuint64_t)p.L, (cuuint64_t)p.S};
+    cuuint64_t strides[3] = {(cuuint64_t)(p.s_y1 * 4), (cuuint64_t)(p.s_y0 * 4), (cuuint64_t)(p.seq_y * 4)};
+    cuuint32_t box[4] = {32, 1, 64, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.y, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Maps of the state kernel: x and B in 64-token boxes (its step).
 bool make_state_maps(EncodeFn fn, TcMaps* m, const ScanParams& p) {
     const int64_t S = p.S;
     std::memset(&m->c, 0, sizeof(m->c));
+    std::memset(&m->y, 0, sizeof(m->y));
+    m->y_ok = 0;
     return make_map(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf) &&
            make_map(fn, &m->b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf);
 }
@@ -1952,6 +2003,8 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* s
         !make_map(fn, &maps.b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b) ||
         !make_map(fn, &maps.c, p.C, p.N, p.G, p.L, S, p.s_c1, p.s_c0, p.seq_c))
         return cudaErrorInvalidValue;
+    maps.y_ok = make_y_map(fn, &maps.y, p) ? 1 : 0;
+    if (!maps.y_ok) std::memset(&maps.y, 0, sizeof(maps.y));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const char* only = std::getenv("HELIX_ONLY_PASS");
     const bool do_a = !only || *only == 'A';
