@@ -141,6 +141,7 @@ extern "C" helix_status helix_scan_encode_static(helix_ctx* ctx, void* stream, c
     p.agg = reinterpret_cast<float*>(static_cast<char*>(scratch) + pl.off_agg);
     p.lam = reinterpret_cast<float*>(static_cast<char*>(scratch) + pl.off_lam);
     p.tile_flag = pl.has_flags ? reinterpret_cast<int32_t*>(static_cast<char*>(scratch) + pl.off_flag) : nullptr;
+    p.run_span = pl.has_span ? reinterpret_cast<float*>(static_cast<char*>(scratch) + pl.off_span) : nullptr;
 
     const int rc = pl.path == kPathTcBf16 ? launch_tc(ctx, pl, p, stream) : launch_simt(ctx, pl, p, stream);
     if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);

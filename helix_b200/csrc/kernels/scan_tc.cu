@@ -1456,9 +1456,20 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // kernel's span-entry states are read after the wait
         grid_dep_wait();
         if (tid == 0) HX_KS(6);
+        if (p.run_span) {
+            // the state kernel measured every run's largest chunk decay span
+            for (int k = tid; k < 2 * p.out_k; k += kPEpi * 32) {
+                const int v = k / p.out_k, r = pt.run0 + k % p.out_k;
+                const SlabRef& sr = v ? pt.s[1] : pt.s[0];
+                if (sr.valid && r < p.n_runs) {
+                    const float m = p.run_span[((int64_t)pt.seq * p.H + sr.h) * p.n_runs + r];
+                    if (m > 0.0f) atomicMax(&span_bits, __float_as_uint(m));
+                }
+            }
+        }
         load_state_tile(p, pt, st, tid);
         if (tid == 0) HX_TL(24, 0);
-        pair_span(p, pt, warp, kPEpi + kPBld, &span_bits);
+        if (!p.run_span) pair_span(p, pt, warp, kPEpi + kPBld, &span_bits);
         if (tid == 0) HX_TL(25, 0);
     } else if (warp == kPWarpVec) {
         // the chunk vectors of chunk 0 straight into ring slot 0
@@ -1487,7 +1498,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             pre[4 * k + 2] = __uint_as_float(v[k].z);
             pre[4 * k + 3] = __uint_as_float(v[k].w);
         }
-        pair_span(p, pt, kPEpi + bld_index(warp), kPEpi + kPBld, &span_bits);
+        if (!p.run_span) pair_span(p, pt, kPEpi + bld_index(warp), kPEpi + kPBld, &span_bits);
         if (warp == 8 && lane == 0) HX_TL(27, 0);
     }
     __syncthreads();
@@ -1810,6 +1821,7 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
         const int lane = tid & 31;
         float* dtr = reinterpret_cast<float*>(sm + SO_DT);
         float later = 0.0f;  // log2 units: sum of A*dt over chunks after this one
+        float span_mx = 0.0f;  // largest |A| sum dt of a chunk (log2 units)
         auto park = [&](int q, const float (&r)[4]) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) dtr[(q & 3) * 128 + 4 * lane + k] = r[k];
@@ -1828,6 +1840,7 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
             float v[4], pre[4], total;
             if (lane == 0) HX_TLS(13, q);
             warp_chunk_prefix(p, db, t0, min(kCS, t_end - t0), Ah2, raw, v, pre, &total);
+            span_mx = fmaxf(span_mx, fabsf(total));
             if (lane == 0) HX_TLS(14, q);
             const int slot = q % kStRing;
             if (q >= kStRing) {
@@ -1850,6 +1863,30 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
         }
         if (!ok) atomicCAS(&g_tc_fault, 0u, kFaultMmaState);
         if (lane == 0) lam_total = later / kLog2e;
+        if (ok && lane == 0 && p.run_span && tl.slab == 0)
+            p.run_span[((int64_t)tl.seq * p.H + tl.h) * p.n_runs + tl.run] = span_mx;
+        if (ok && p.run_span && tl.slab == 0 && tl.run < p.n_runs - p.state_runs) {
+            // the last output span has no state pass: run state_runs + r of
+            // this head is measured here, four chunks' dt in flight at a time
+            const int r2 = p.state_runs + tl.run;
+            const int tb = r2 * p.run_tok, te = min(p.L, tb + p.run_tok);
+            const int nc = (te - tb + kCS - 1) / kCS;
+            float mx = 0.0f;
+#pragma unroll 1
+            for (int q0 = 0; q0 < nc; q0 += 4) {
+                float raw[4][4];
+#pragma unroll
+                for (int b = 0; b < 4; ++b) warp_load_dt(p, db, tb + min(q0 + b, nc - 1) * kCS, te, raw[b]);
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int t0 = tb + min(q0 + b, nc - 1) * kCS;
+                    float v[4], pre[4], total;
+                    warp_chunk_prefix(p, db, t0, min(kCS, te - t0), Ah2, raw[b], v, pre, &total);
+                    mx = fmaxf(mx, fabsf(total));
+                }
+            }
+            if (lane == 0) p.run_span[((int64_t)tl.seq * p.H + tl.h) * p.n_runs + r2] = mx;
+        }
         __syncwarp();
     } else {
         // ---- xw builders: two 16-byte x vectors per thread per step -------

@@ -187,6 +187,9 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     // The tensor-core output kernels record per tile which path ran, so the
     // general-path kernel need not re-measure the decay spans.
     pl.has_flags = d.multipass && pl.path == kPathTcBf16;
+    // ... and, when a state pass runs, the largest decay span of every run's
+    // chunks, measured there, so the output kernel need not read dt for it.
+    pl.has_span = pl.has_flags && pl.need_state_kernel;
     if (pl.run_slots > 0 || pl.has_flags) {
         const size_t agg = (size_t)d.n_seq * d.n_head * pl.run_slots * d.head_dim * d.d_state;
         const size_t lam = (size_t)d.n_seq * d.n_head * pl.run_slots;
@@ -195,7 +198,9 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
         pl.off_agg = 0;
         pl.off_lam = align256(agg * sizeof(float));
         pl.off_flag = pl.off_lam + align256(lam * sizeof(float));
-        pl.total = pl.off_flag + align256(tiles * sizeof(int32_t));
+        const size_t spans = pl.has_span ? (size_t)d.n_seq * d.n_head * pl.n_runs : 0;
+        pl.off_span = pl.off_flag + align256(tiles * sizeof(int32_t));
+        pl.total = pl.off_span + align256(spans * sizeof(float));
     }
     return pl;
 }

@@ -110,6 +110,7 @@ helix_status encode_core(helix_ctx* ctx, void* stream, const helix_scan_desc* d,
         p.agg = reinterpret_cast<float*>(at<char>(scratch) + pl.off_agg);
         p.lam = reinterpret_cast<float*>(at<char>(scratch) + pl.off_lam);
         p.tile_flag = pl.has_flags ? reinterpret_cast<int32_t*>(at<char>(scratch) + pl.off_flag) : nullptr;
+        p.run_span = pl.has_span ? reinterpret_cast<float*>(at<char>(scratch) + pl.off_span) : nullptr;
     }
 
     if (pl.path == hx::kPathTcBf16) {

@@ -62,6 +62,8 @@ struct Plan {
     size_t off_lam  = 0;    // f32 [seq][head][run_slots]
     size_t off_flag = 0;    // i32 [output tiles] (tensor-core family, multipass): fast path taken
     bool   has_flags = false;
+    size_t off_span = 0;    // f32 [seq][head][n_runs]: largest decay span of a run's chunks
+    bool   has_span = false; // written by the state kernel (tensor-core family with a state pass)
     size_t total    = 0;    // scratch bytes
 };
 
@@ -95,6 +97,7 @@ struct ScanParams {
     float*         agg;     // scratch, see Plan
     float*         lam;
     int32_t*       tile_flag;  // scratch or null, see Plan
+    float*         run_span;   // scratch or null, see Plan
 };
 
 }  // namespace hx
