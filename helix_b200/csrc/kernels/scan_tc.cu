@@ -1407,6 +1407,21 @@ __device__ __forceinline__ void pair_span(const ScanParams& p, const PairTile& p
     }
     if (lane == 0 && mx > 0.0f) atomicMax(span_bits, __float_as_uint(mx));
 }
+// The largest chunk decay span of a tile from the state pass's per-run
+// record (float bits; spans are >= 0, so their bit patterns order as floats).
+__device__ __forceinline__ unsigned tile_span_bits(const ScanParams& p, const PairTile& pt) {
+    unsigned bits = 0u;
+    for (int k = 0; k < 2 * p.out_k; ++k) {
+        const int v = k / p.out_k, r = pt.run0 + k % p.out_k;
+        const SlabRef& sr = v ? pt.s[1] : pt.s[0];
+        if (sr.valid && r < p.n_runs) {
+            // L2, not L1: the general kernel reads this before its grid wait
+            const float m = __ldcg(p.run_span + ((int64_t)pt.seq * p.H + sr.h) * p.n_runs + r);
+            if (m > 0.0f) bits = max(bits, __float_as_uint(m));
+        }
+    }
+    return bits;
+}
 __device__ __forceinline__ bool pair_takes_fast(const ScanParams& p, unsigned span_bits, int force_general) {
     return !force_general && (p.P & 7) == 0 && __uint_as_float(span_bits) <= kFastSpan2;
 }
@@ -1456,17 +1471,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // kernel's span-entry states are read after the wait
         grid_dep_wait();
         if (tid == 0) HX_KS(6);
-        if (p.run_span) {
-            // the state kernel measured every run's largest chunk decay span
-            for (int k = tid; k < 2 * p.out_k; k += kPEpi * 32) {
-                const int v = k / p.out_k, r = pt.run0 + k % p.out_k;
-                const SlabRef& sr = v ? pt.s[1] : pt.s[0];
-                if (sr.valid && r < p.n_runs) {
-                    const float m = p.run_span[((int64_t)pt.seq * p.H + sr.h) * p.n_runs + r];
-                    if (m > 0.0f) atomicMax(&span_bits, __float_as_uint(m));
-                }
-            }
-        }
+        // the state kernel measured every run's largest chunk decay span
+        if (p.run_span && tid == 0) span_bits = tile_span_bits(p, pt);
         load_state_tile(p, pt, st, tid);
         if (tid == 0) HX_TL(24, 0);
         if (!p.run_span) pair_span(p, pt, warp, kPEpi + kPBld, &span_bits);
@@ -1537,6 +1543,15 @@ __global__ void __launch_bounds__(kOutThreads, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const PairTile pt = pair_tile(p);
+    if (p.run_span && blockIdx.x != 0) {
+        // The fast kernel's decision, taken again from the same record: the
+        // state pass wrote it before the carry kernel's wait returned, and
+        // this grid starts only after every fast-kernel CTA has started, so
+        // after that wait.  A tile the fast kernel keeps needs nothing from
+        // this grid; CTA 0 always waits, so this grid still ends after the
+        // fast kernel's.
+        if (pair_takes_fast(p, tile_span_bits(p, pt), force_general)) return;
+    }
     grid_dep_wait();  // the fast kernel's records and outputs
     if (tid == 0) {
         for (int k = 0; k < 4; ++k) mbar_init(&cb_bar[k], 1);
