@@ -67,3 +67,25 @@ def test_ctx_create_reports_no_device_here():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(RuntimeError):
         abi.load(tmp_path / "libhelix.so")
+
+
+def test_tensor_core_scratch_plan_c3():
+    """BASELINE config 3 (bf16 operands, multipass) on a 148-SM part: spans of
+    16 chunks (4 output spans, 128 pair tiles), 2 runs per span chosen by the
+    state kernel's cost model, so 6 run states per head are kept, plus one
+    log-decay per run state, one path record per output tile and one decay
+    span per run (8 per head), each region 256-byte aligned."""
+    lib = abi.load()
+    d = abi.desc_init(8192, 1, 64, 64, 128, 8)
+    d.io_dtype = 2  # HELIX_BF16
+    d.compute_dtype = 2
+    d.multipass = True
+
+    def al(n):
+        return (n + 255) // 256 * 256
+
+    agg = 64 * 6 * 64 * 128 * 4
+    lam = al(64 * 6 * 4)
+    flags = al(8 * 4 * 4 * 4)
+    spans = al(64 * 8 * 4)
+    assert lib.helix_scan_scratch_size(None, C.byref(d)) == agg + lam + flags + spans
