@@ -725,7 +725,8 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
 //
 // which is exact algebra; the scaling factors stay inside fp32/bf16 range
 // while no chunk of the span decays by more than kFastSpan2 (log2 units),
-// which the kernel prologue checks for both slabs (tiles that fail go to
+// which the kernel prologue checks for both slabs, from the state pass's
+// per-run record when there is one (tiles that fail go to
 // tc_out_general_kernel).  The chunk's MMAs, all N = 128:
 //
 //   G1    D1[t][j]   = C . B^T              A = C (K-major)     B = B (K-major)
@@ -734,7 +735,9 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
 //   G2^T  Y[c][t]   += xw_hi^T . mask^T     A = xw (MN-major)   B = mask (K-major)
 //
 // with c the channel of either slab (TMEM lane), so y leaves TMEM with
-// consecutive lanes on consecutive channels: coalesced stores, no staging.
+// consecutive lanes on consecutive channels: 128-byte token rows of 32
+// channels, staged in the chunk's C/B stage (free once G2 retired) and
+// written by one TMA store per warp.
 // The causal mask (D1 with j > t zeroed, bf16) is written over the chunk's C
 // once G3 has read it; the carried state lives in the G4 accumulator D4 (the
 // epilogue scales it to S~ in place and leaves a bf16 copy as G3's operand).
@@ -743,7 +746,7 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
 //   warps 0-7     epilogue, lane quarter w & 3, column half w >> 2, per chunk:
 //                 the mask of D1(i) -> smem over C(i) (after G3(i)); S_{i+1}
 //                 -> S~_{i+1} in D4 and its bf16 copy (after G4(i)); y(i) =
-//                 f_t Y -> global (after G2(i)), one 128-byte row per store;
+//                 f_t Y -> C/B stage of chunk i -> TMA store (after G2(i));
 //                 s1 after the span's last chunk, through shared memory
 //   warps 8, 9, 11, 12, 13, 15   xw = w x as bf16 hi | lo (x one chunk
 //                 ahead in registers): lo once G4(i-1) retired, hi once
