@@ -135,6 +135,27 @@ def test_strided_y_bf16(ctx, oracle, y_view):
     check_bf16(f"bf16 strided y {y_view.__name__}", y, s1, y_ref, s_ref)
 
 
+@pytest.mark.parametrize("span", [1, 3], ids=["inner_span", "last_span"])
+def test_fast_general_decision_from_state_pass(ctx, oracle, run_tokens, span):
+    """With a state pass, the output kernels take the fast/general decision
+    from the decay spans the state pass records per run: for the runs it
+    reduces, and for the last output span (which it does not reduce) from an
+    extra measurement.  One chunk of head 0 decays by hundreds of nats inside
+    the given span; the fast path's rescaling factors would overflow there,
+    so only a tile sent down the general path gives finite, correct output."""
+    shape = (2048, 1, 4, 64, 128, 2)
+    prob = oracle.harness_problem(*shape, 4242, True)
+    t0 = 512 * span + 128
+    prob["dt"][:, t0:t0 + 128, 0] = 6.0  # softplus(6) ~ 6 per token
+    prob = widen(prob, "bf16")
+    y_ref, s_ref = _oracle(oracle, prob, shape)
+    run_tokens("512")  # four output spans of one run each: a state pass over runs 0..2
+    y, s1, d = run(ctx, prob, multipass=True, io="bf16", compute="bf16")
+    assert "tcgen05" in ctx.backend_desc(d)
+    assert np.isfinite(y).all() and np.isfinite(s1).all()
+    check_bf16(f"bf16 decision from state pass span {span}", y, s1, y_ref, s_ref)
+
+
 def test_c3_full_size_bf16(ctx, oracle):
     """BASELINE config 3 at full size on the BASELINE distributions."""
     from helix_b200.synth import Shape, make_inputs, to_numpy_f32
