@@ -8,6 +8,38 @@
 
 namespace hx {
 
+// Codes of the device fault word (helix_device_fault): the first event
+// recorded since the word was last read.
+enum : unsigned {
+    kFaultTmaOut = 1,      // output kernel: a TMA arrival wait ran out
+    kFaultMmaOut = 2,      // output kernel: an MMA / hand-off wait ran out
+    kFaultTmaState = 3,    // state kernel: a TMA arrival wait ran out
+    kFaultMmaState = 4,    // state kernel: an MMA / hand-off wait ran out
+    kFaultIdsOverlap = 5,  // an s0 row selected by ids overlaps the s1 rows written
+};
+
+constexpr float kNaN = __builtin_nanf("");
+
+// Row of s0 that sequence seq starts from: ids[seq], or seq without ids.
+// Returns false, and records kFaultIdsOverlap, when ids selects a row whose
+// bytes overlap the s1 rows this call writes (other CTAs may be writing
+// them while it is read); the caller then starts the sequence from NaN, so
+// its outputs come out NaN instead of silently wrong.  Overlap with the
+// first n_seq rows of s0 is rejected on the host before anything runs; this
+// covers the rows only ids reaches.
+__device__ __forceinline__ bool s0_row(const ScanParams& p, int seq, int* src) {
+    const int r = p.has_ids ? p.ids[seq] : seq;
+    *src = r;
+    if (!p.has_ids) return true;
+    const char* a = reinterpret_cast<const char*>(p.s0 + (int64_t)r * p.seq_s);
+    const char* w = reinterpret_cast<const char*>(p.s1);
+    if (a < w + p.s1_bytes && w < a + p.s_row_bytes) {
+        if (p.fault) atomicCAS(p.fault, 0u, kFaultIdsOverlap);
+        return false;
+    }
+    return true;
+}
+
 // log(1 + e^v) for v <= 20 as max(v, 0) + log1p(u), u = e^-|v| in (0, 1],
 // with log1p(u) = 2 atanh(s) = 2 (s + s^3/3 + s^5/5 + ... + s^15/15),
 // s = u / (2 + u) <= 1/3 (the Taylor series of atanh; the first omitted term

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include "../runtime/internal.h"
+#include "common.cuh"
 
 namespace hx {
 namespace {
@@ -61,8 +62,9 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t e = gid - head_lin * per_head;
     const int seq = (int)(head_lin / p.H), h = (int)(head_lin % p.H);
     const int c = (int)(e / p.N), n = (int)(e % p.N);
-    const int src = p.has_ids ? p.ids[seq] : seq;
-    float S = p.s0[(int64_t)src * p.seq_s + (int64_t)h * p.s_s0 + (int64_t)c * p.s_s1 + n];
+    int src;
+    float S = s0_row(p, seq, &src) ? p.s0[(int64_t)src * p.seq_s + (int64_t)h * p.s_s0 + (int64_t)c * p.s_s1 + n]
+                                   : kNaN;
     const int64_t n_heads = (int64_t)p.S * p.H;
     for (int j = 0; j < n_prev; ++j)
         S = fmaf(expf(ld[(int64_t)j * n_heads + head_lin]), S, states[(int64_t)j * n_state + gid]);

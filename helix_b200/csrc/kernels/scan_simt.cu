@@ -191,11 +191,12 @@ __global__ void __launch_bounds__(kThreads, 1) simt_out_kernel(ScanParams p) {
 
     // ---- state entering this run --------------------------------------
     {
-        const int src = p.has_ids ? p.ids[tl.seq] : tl.seq;
+        int src;
+        const bool clear = s0_row(p, tl.seq, &src);
         const float* s0 = p.s0 + (int64_t)src * p.seq_s + (int64_t)tl.h * p.s_s0 + (int64_t)p0 * p.s_s1;
         for (int i = tid; i < NMAX * kSlab; i += kThreads) {
             const int c = i / NMAX, n = i - c * NMAX;
-            Ss[n * kXs + c] = (c < pw && n < N) ? s0[(int64_t)c * p.s_s1 + n] : 0.0f;
+            Ss[n * kXs + c] = (c < pw && n < N) ? (clear ? s0[(int64_t)c * p.s_s1 + n] : kNaN) : 0.0f;
         }
         // The carry loop below maps threads to (c, n) differently when
         // N < NMAX, so the fill must be complete first.

@@ -9,27 +9,30 @@
 // helix_scan_encode wants a caller-provided scratch buffer; those callers have
 // no way to provide one.
 //
-// What it costs: the array below, kStaticScratchBytes (32 MiB), lives on every
-// GPU that loads this library until the process exits, whether or not the
-// entry point is ever called.
+// What it costs: the array below, kStaticScratchBytes (32 MiB) on each device.
+// CUDA loads the code module that holds it (and reserves the 32 MiB) when the
+// first call on a device asks for the array's address -- with lazy module
+// loading, CUDA's default, not before.  From then on the device keeps it
+// until the process exits.
 //
 // Rules for callers:
-//   * The first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (with that device current).  Make that first call
-//     before any stream capture.
+//   * Make the first call on each device at start-up, before any stream
+//     capture: it loads the array.  If the device has no room left for it,
+//     that call fails with HELIX_ERR_PIPELINE and says so, and nothing is
+//     enqueued.
 //   * Every call on a device uses the same array.  Two calls whose work can
 //     overlap on the GPU (other streams, other threads, other contexts on the
 //     same device) race on it and produce wrong results; serialise them.
 //   * The array keeps whatever the last call left in it.  No part of it needs
-//     to start at zero: each call's state kernel writes every run state and
-//     run decay before the same call's output kernel reads them.
+//     to start at zero: each call's state kernel writes every run state, run
+//     decay and run decay span, and its fast output kernel every tile flag,
+//     before the same call's later kernels read them.
 //   * A descriptor whose multipass scratch (helix_scan_scratch_size with
 //     multipass = true) exceeds kStaticScratchBytes is rejected with
 //     HELIX_ERR_SCRATCH_TOO_SMALL and a message; nothing is enqueued.
 //   * Nothing here calls cudaMalloc, cudaFree or any allocating routine.
 #include <cuda_runtime.h>
 
-#include <mutex>
 #include <string>
 
 #include "../runtime/internal.h"
@@ -39,32 +42,8 @@ namespace hx {
 namespace {
 
 constexpr size_t kStaticScratchBytes = (size_t)32 << 20;
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
-
-std::mutex g_static_mu;
-void* g_static_ptr[kMaxDevices] = {};
-
-// Device address of g_static_scratch on `dev` (which must be current).
-// Looked up once per device.
-cudaError_t static_scratch_on(int dev, void** out) {
-    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> lk(g_static_mu);
-    if (!g_static_ptr[dev]) {
-        void* ptr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
-        if (e != cudaSuccess) return e;
-        g_static_ptr[dev] = ptr;
-    }
-    *out = g_static_ptr[dev];
-    return cudaSuccess;
-}
-
-template <class T>
-T* at(helix_tensor t) {
-    return reinterpret_cast<T*>(static_cast<char*>(t.buf) + t.offset);
-}
 
 }  // namespace
 }  // namespace hx
@@ -95,59 +74,30 @@ extern "C" helix_status helix_scan_encode_static(helix_ctx* ctx, void* stream, c
                            " (use helix_scan_encode with caller scratch)");
         return HELIX_ERR_SCRATCH_TOO_SMALL;
     }
-    {
-        const uintptr_t a0 = reinterpret_cast<uintptr_t>(at<char>(s0));
-        const uintptr_t b0 = reinterpret_cast<uintptr_t>(at<char>(s1));
-        const int64_t last = (int64_t)(d.n_seq - 1) * d.seq_s + (int64_t)(d.n_head - 1) * d.s_s[0] +
-                             (int64_t)(d.head_dim - 1) * d.s_s[1] + (int64_t)(d.d_state - 1);
-        const uintptr_t span = (uintptr_t)(last + 1) * sizeof(float);
-        if (a0 < b0 + span && b0 < a0 + span) {
-            set_error(ctx, "s0 and s1 overlap");
-            return HELIX_ERR_INVALID_ARG;
-        }
-    }
-    if (pl.path == kPathTcBf16) {
-        const uintptr_t m = reinterpret_cast<uintptr_t>(at<char>(x)) | reinterpret_cast<uintptr_t>(at<char>(B)) |
-                            reinterpret_cast<uintptr_t>(at<char>(C));
-        if (m & 15) {
-            set_error(ctx, "x, B and C must be 16-byte aligned for the tensor-core path");
-            return HELIX_ERR_UNSUPPORTED_SHAPE;
-        }
-    }
+    ScanParams p{};
+    const CallTensors t{s0, x, dt, A, B, C, ids, y, s1};
+    const helix_status st = bind_call(ctx, d, pl, t, &p);
+    if (st != HELIX_OK) return st;
 
+    // The array's device address on ctx's device, looked up on every call
+    // (cheap once the module is loaded; a cached address would dangle after
+    // a device reset reloads the module elsewhere).  The lookup needs the
+    // device current.
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != ctx->device) cudaSetDevice(ctx->device);
     void* scratch = nullptr;
-    const cudaError_t se = static_scratch_on(ctx->device, &scratch);
-    if (se != cudaSuccess) {
-        if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);
-        set_error(ctx, std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(se));
-        return HELIX_ERR_PIPELINE;
-    }
-
-    ScanParams p{};
-    fill_params(p, d, pl);
-    p.has_ids = ids.buf ? 1 : 0;
-    p.x = at<void>(x);
-    p.dt = at<float>(dt);
-    p.A = at<float>(A);
-    p.B = at<void>(B);
-    p.C = at<void>(C);
-    p.ids = ids.buf ? at<int32_t>(ids) : nullptr;
-    p.s0 = at<float>(s0);
-    p.y = at<float>(y);
-    p.s1 = at<float>(s1);
-    p.agg = reinterpret_cast<float*>(static_cast<char*>(scratch) + pl.off_agg);
-    p.lam = reinterpret_cast<float*>(static_cast<char*>(scratch) + pl.off_lam);
-    p.tile_flag = pl.has_flags ? reinterpret_cast<int32_t*>(static_cast<char*>(scratch) + pl.off_flag) : nullptr;
-    p.run_span = pl.has_span ? reinterpret_cast<float*>(static_cast<char*>(scratch) + pl.off_span) : nullptr;
-
-    const int rc = pl.path == kPathTcBf16 ? launch_tc(ctx, pl, p, stream) : launch_simt(ctx, pl, p, stream);
+    const cudaError_t se = cudaGetSymbolAddress(&scratch, g_static_scratch);
     if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);
-    if (rc != cudaSuccess) {
-        set_error(ctx, std::string("kernel launch failed: ") + cudaGetErrorString(static_cast<cudaError_t>(rc)));
+    if (se != cudaSuccess) {
+        cudaGetLastError();
+        set_error(ctx, se == cudaErrorMemoryAllocation
+                           ? std::string("helix_scan_encode_static: out of device memory loading its ") +
+                                 std::to_string(kStaticScratchBytes >> 20) +
+                                 " MiB scratch array (make the first call at start-up)"
+                           : std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(se));
         return HELIX_ERR_PIPELINE;
     }
-    return HELIX_OK;
+    bind_scratch(pl, static_cast<char*>(scratch), &p);
+    return run_call(ctx, pl, p, stream);
 }

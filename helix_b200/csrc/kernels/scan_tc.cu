@@ -26,65 +26,6 @@
 #include "common.cuh"
 #include "umma.cuh"
 
-// Phase markers for cycle attribution.  They expand to nothing in the
-// library; a profiling build that defines HX_PHASE_PROFILE provides
-// hx_phase_cycles[] and accumulates thread 0's SM cycles between markers.
-#ifdef HX_PHASE_PROFILE
-extern __device__ unsigned long long hx_phase_cycles[32];
-#define HX_PHASE_START long long hx_phase_t = clock64()
-#define HX_PHASE(k) HX_PHASE_T(k, 0)
-#define HX_PHASE_T(k, who)                                            \
-    do {                                                              \
-        if (threadIdx.x == (who)) {                                   \
-            const long long now_ = clock64();                         \
-            atomicAdd(&hx_phase_cycles[k], (unsigned long long)(now_ - hx_phase_t)); \
-            hx_phase_t = now_;                                        \
-        }                                                             \
-    } while (0)
-// Timeline of one CTA (blockIdx.x == HX_TL_CTA): clock64 of event `ev` in
-// chunk `i`.
-extern __device__ long long hx_tl[32 * 64];
-extern __device__ unsigned long long hx_cta[1024 * 4];
-__device__ __forceinline__ unsigned long long hx_gtime() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-#define HX_CTA(k) do { if (threadIdx.x == 0 && blockIdx.x < 1024) hx_cta[blockIdx.x * 4 + (k)] = hx_gtime(); } while (0)
-#define HX_CTA_T(k) do { if (blockIdx.x < 1024) hx_cta[blockIdx.x * 4 + (k)] = hx_gtime(); } while (0)
-// State-kernel timeline of CTAs 40 and 340: globaltimer of event `ev` at
-// step `i`.
-extern __device__ unsigned long long hx_tls[2 * 16 * 64];
-#define HX_TLS(ev, i)                                                                          \
-    do {                                                                                       \
-        if ((blockIdx.x == 40 || blockIdx.x == 340) && (i) < 64)                                \
-            hx_tls[(blockIdx.x == 340) * 1024 + (ev) * 64 + (i)] = hx_gtime();                  \
-    } while (0)
-// Grid-wide spans: earliest event `k` (slot 2k) and latest (slot 2k+1) over
-// the CTAs that reach it.
-extern __device__ unsigned long long hx_kspan[32];
-#define HX_KS(k)                                                  \
-    do {                                                          \
-        const unsigned long long t_ = hx_gtime();                 \
-        atomicMin(&hx_kspan[2 * (k)], t_);                        \
-        atomicMax(&hx_kspan[2 * (k) + 1], t_);                    \
-    } while (0)
-#define HX_TL_CTA 40
-#define HX_TL(ev, i)                                                          \
-    do {                                                                      \
-        if (blockIdx.x == HX_TL_CTA && (i) < 64) hx_tl[(ev) * 64 + (i)] = clock64(); \
-    } while (0)
-#else
-#define HX_TL(ev, i) do {} while (0)
-#define HX_CTA(k) do {} while (0)
-#define HX_CTA_T(k) do {} while (0)
-#define HX_TLS(ev, i) do {} while (0)
-#define HX_KS(k) do {} while (0)
-#define HX_PHASE_START do {} while (0)
-#define HX_PHASE(k) do {} while (0)
-#define HX_PHASE_T(k, who) do {} while (0)
-#endif
-
 namespace hx {
 
 // Device-side fault word: 0 = none, else the code of the first bounded wait
@@ -98,7 +39,6 @@ using namespace umma;
 constexpr int kCS = 128;
 constexpr long long kWaitBudget = 1ll << 31;  // clock cycles, ~1 s
 
-enum : unsigned { kFaultTmaOut = 1, kFaultMmaOut = 2, kFaultTmaState = 3, kFaultMmaState = 4 };
 
 struct TcMaps {
     CUtensorMap x, b, c;
@@ -335,7 +275,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
     __shared__ OutBars bars_all[2];
     OutBars& bars = bars_all[set];
 
-    HX_PHASE_START;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int role = warp < 4 ? kRoleY : warp < 12 ? kRoleM : warp < 16 ? kRoleC : kRoleXW;  // 16-17 XW
     const int row = 32 * (warp & 3) + lane;
@@ -387,7 +326,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
             // C/B of chunks 0 and 1 are already in flight (kernel prologue)
             for (int i = 0; i < 2 && i < n_ch; ++i) load_x(i);
             const uint32_t aXH = smem_u32(sXW), aXL = aXH + 16384, aS = smem_u32(sS);
-            HX_PHASE_T(16, 32 * kGWarpMma);
             for (int i = 0; i <= n_ch && ok; ++i) {
                 if (i < n_ch) {
                     const uint32_t par = (uint32_t)(i & 1), pf = (uint32_t)((i >> 1) & 1);
@@ -398,7 +336,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                         if (!(ok = mbar_wait(&bars.d1_read, par ^ 1u, kWaitBudget))) break;
                         if (!(ok = mbar_wait(&bars.d4_read, par ^ 1u, kWaitBudget))) break;
                     }
-                    HX_PHASE_T(17, 32 * kGWarpMma);
                     tc_fence_after();
                     const uint32_t aC = smem_u32(sCB(i)), aB = aC + 32768;
 #pragma unroll
@@ -412,7 +349,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                         mma_bf16(tm + T_D4, desc_mnmajor(aB, ks), desc_mnmajor(aXL, ks), ID_G4, 1);
                     mma_commit(&bars.acc1);
                     mma_commit(&bars.xw_free);
-                    HX_PHASE_T(18, 32 * kGWarpMma);
                 }
                 if (i > 0) {
                     const int k = i - 1;  // G2 of the previous chunk
@@ -420,7 +356,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                     if (k > 0) {
                         if (!(ok = mbar_wait(&bars.d_free, (uint32_t)((k - 1) & 1), kWaitBudget))) break;
                     }
-                    HX_PHASE_T(19, 32 * kGWarpMma);
                     tc_fence_after();
                     const uint32_t aX = smem_u32(sX(k));
 #pragma unroll
@@ -436,7 +371,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                 if (i < n_ch) {
                     const uint32_t par = (uint32_t)(i & 1);
                     if (!(ok = mbar_wait(&bars.s_ready, par, kWaitBudget))) break;  // S_i in smem
-                    HX_PHASE_T(20, 32 * kGWarpMma);
                     tc_fence_after();
                     const uint32_t aC = smem_u32(sCB(i));
 #pragma unroll
@@ -449,7 +383,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                         if (!(ok = mbar_wait(&bars.g3, par, kWaitBudget))) break;
                         load_cb(i + 2);
                     }
-                    HX_PHASE_T(21, 32 * kGWarpMma);
                 }
             }
             if (!ok) {
@@ -504,7 +437,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
             if (i > 0) {
                 if (!(ok = role_wait(&bars.xw_free, (uint32_t)((i - 1) & 1), role, kFaultMmaOut, leader))) break;
             }
-            HX_PHASE_T(22, 512);
             const float* wv = slot(i) + 256;
             const uint8_t* x = sX(i);
 #pragma unroll 4
@@ -524,7 +456,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                 mbar_arrive(&bars.xw_ready);
                 mbar_arrive(&bars.v_empty[i % kRing]);
             }
-            HX_PHASE_T(23, 512);
         }
     } else if (role == kRoleM) {
         // ================= W_m: M' into TMEM ================================
@@ -533,7 +464,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
         for (int i = 0; i < n_ch; ++i) {
             if (!(ok = role_wait(&bars.acc1, (uint32_t)(i & 1), role, kFaultMmaOut, leader))) break;
             if (!(ok = role_wait(&bars.v_full[i % kRing], (uint32_t)((i / kRing) & 1), role, kFaultMmaOut, leader))) break;
-            HX_PHASE_T(24, 128);
             tc_fence_after();
             const float* vs = slot(i);
             const float* Lc2 = vs + 128;
@@ -586,7 +516,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                 mbar_arrive(&bars.m_ready);
                 mbar_arrive(&bars.v_empty[i % kRing]);
             }
-            HX_PHASE_T(25, 128);
         }
     } else if (role == kRoleC) {
         // ================= W_c: the carry, fp32 state in TMEM ===============
@@ -596,8 +525,10 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
             const float* src;
             int64_t sc;
             if (ot.run0 == 0) {
-                const int sq = p.has_ids ? p.ids[tl.seq] : tl.seq;
-                src = p.s0 + (int64_t)sq * p.seq_s + (int64_t)tl.h * p.s_s0 + (int64_t)p0 * p.s_s1 + row;
+                int sq;
+                src = s0_row(p, tl.seq, &sq) ? p.s0 + (int64_t)sq * p.seq_s + (int64_t)tl.h * p.s_s0 +
+                                                   (int64_t)p0 * p.s_s1 + row
+                                             : nullptr;
                 sc = p.s_s1;
             } else {
                 src = p.agg + (unit0 + ot.run0 - 1) * (int64_t)p.P * p.N + (int64_t)p0 * p.N + row;
@@ -607,7 +538,8 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
             for (int q = 0; q < 8; ++q) {
                 float v[8];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = (8 * q + k < pw) ? src[(int64_t)(8 * q + k) * sc] : 0.0f;
+                for (int k = 0; k < 8; ++k)
+                    v[k] = (8 * q + k < pw) ? (src ? src[(int64_t)(8 * q + k) * sc] : __int_as_float(0x7fc00000)) : 0.0f;
                 tmem_st8(tS + 8 * q, *reinterpret_cast<const uint32_t(*)[8]>(v));
                 *reinterpret_cast<uint4*>(sS + sw128_off(row, q)) =
                     make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
@@ -620,7 +552,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
         for (int i = 0; i < n_ch; ++i) {
             if (!(ok = role_wait(&bars.acc1, (uint32_t)(i & 1), role, kFaultMmaOut, leader))) break;
             if (!(ok = role_wait(&bars.v_full[i % kRing], (uint32_t)((i / kRing) & 1), role, kFaultMmaOut, leader))) break;
-            HX_PHASE_T(26, 384);
             tc_fence_after();
             const float decay = ex2(slot(i)[128 + kCS - 1]);
             // S_{i+1} = decay S_i + D4(i): fp32 in TMEM, bf16 copy kept in registers
@@ -652,7 +583,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                     make_uint4(sb[4 * c], sb[4 * c + 1], sb[4 * c + 2], sb[4 * c + 3]);
             fence_async_smem();
             warp_arrive(&bars.s_ready);
-            HX_PHASE_T(27, 384);
         }
         if (ok && ot.last) {
             float* s1 = p.s1 + (int64_t)tl.seq * p.seq_s + (int64_t)tl.h * p.s_s0 + (int64_t)p0 * p.s_s1 + row;
@@ -675,7 +605,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
             // per-buffer barrier: G3(i+1) may retire before this wait, G3(i+2) may not
             if (!(ok = role_wait(&bars.g3y[i & 1], (uint32_t)((i >> 1) & 1), role, kFaultMmaOut, leader))) break;
             if (!(ok = role_wait(&bars.v_full[i % kRing], (uint32_t)((i / kRing) & 1), role, kFaultMmaOut, leader))) break;
-            HX_PHASE(28);
             tc_fence_after();
             const int tp = t_begin + i * kCS;
             const int tlen = t_end - tp;
@@ -709,7 +638,6 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                 mbar_arrive(&bars.d_free);
                 mbar_arrive(&bars.v_empty[i % kRing]);
             }
-            HX_PHASE(29);
         }
     }
 }
@@ -857,7 +785,8 @@ __device__ __forceinline__ float4* st_vec(float* st, int r, int m) {
 // 256 epilogue threads (et = 0..255) with coalesced loads: s0[ids[seq]] for
 // the first span, the carry kernel's slot otherwise; zero past the slab.
 __device__ __forceinline__ void load_state_tile(const ScanParams& p, const PairTile& pt, float* st, int et) {
-    const int sq = p.has_ids ? p.ids[pt.seq] : pt.seq;
+    int sq = 0;
+    const bool clear = pt.run0 != 0 || s0_row(p, pt.seq, &sq);
     const float* src[2];
 #pragma unroll
     for (int v = 0; v < 2; ++v) {
@@ -875,8 +804,9 @@ __device__ __forceinline__ void load_state_tile(const ScanParams& p, const PairT
             for (int m = 0; m < 8; ++m) {
                 const int i4 = et + 256 * (8 * h + m), r = i4 >> 5, n = 4 * (i4 & 31), c = r & 63;
                 const int pw = h ? pt.s[1].pw : pt.s[0].pw;
-                f[m] = c < pw ? __ldg(reinterpret_cast<const float4*>(src[h] + (int64_t)c * rs + n))
-                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                f[m] = c >= pw  ? make_float4(0.0f, 0.0f, 0.0f, 0.0f)
+                       : clear ? __ldg(reinterpret_cast<const float4*>(src[h] + (int64_t)c * rs + n))
+                               : make_float4(kNaN, kNaN, kNaN, kNaN);
             }
 #pragma unroll
             for (int m = 0; m < 8; ++m) {
@@ -892,7 +822,7 @@ __device__ __forceinline__ void load_state_tile(const ScanParams& p, const PairT
             for (int m = 0; m < 32; ++m) {
                 const int idx = et + 256 * (32 * h + m), r = idx >> 7, n = idx & 127, c = r & 63;
                 const int pw = h ? pt.s[1].pw : pt.s[0].pw;
-                f[m] = c < pw ? __ldg(src[h] + (int64_t)c * rs + n) : 0.0f;
+                f[m] = c >= pw ? 0.0f : clear ? __ldg(src[h] + (int64_t)c * rs + n) : kNaN;
             }
 #pragma unroll
             for (int m = 0; m < 32; ++m) {
@@ -987,26 +917,21 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 const uint64_t dC = sdesc_sw128(aC, 16, 1024);              // C, then the mask (K-major)
                 const uint64_t dBm = sdesc_sw128(aC + 32768, 16384, 1024);  // B as MN-major
                 if (!(ok = mbar_wait(&bars.s_ready, par, kWaitBudget))) break;
-                HX_TL(0, i);
                 if (i >= 1 && !(ok = mbar_wait(&bars.y_free, (uint32_t)((i - 1) & 1), kWaitBudget))) break;
-                HX_TL(1, i);
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
                     mma_bf16_ts(tm + TP_Y, tm + TP_S + 8u * (uint32_t)ks, desc_add(dC, kmajor_off(ks)), ID_P_KK, ks > 0);
                 mma_commit(&bars.g3);
-                HX_TL(2, i);
                 if (i >= 1 && i + 1 < n_ch) {
                     // chunk i+1's C/B into chunk i-1's stage once y(i-1),
                     // staged there after G2(i-1), has left it
                     if (!(ok = mbar_wait(&bars.ys_free, (uint32_t)((i - 1) & 1), kWaitBudget))) break;
-                    HX_TL(8, i);
                     load_cb_chunk(maps, sm + OO_CB + 65536u * (uint32_t)((i + 1) & 1), &cb_bar[(i + 1) & 1], pt.g,
                                   t_begin + (i + 1) * kCS, pt.seq);
                     cb_issued = i + 2;
                 }
                 if (!(ok = mbar_wait(&bars.xw_ready, par, kWaitBudget))) break;
-                HX_TL(3, i);
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
@@ -1015,17 +940,13 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 for (int ks = 0; ks < 8; ++ks)
                     mma_bf16(tm + TP_D4, desc_add(dXl, 2048u * ks), desc_add(dBm, 2048u * ks), ID_P_MM, 1u);
                 mma_commit(&bars.g4);
-                HX_TL(4, i);
                 if (!(ok = mbar_wait(&bars.m_ready, par, kWaitBudget))) break;
-                HX_TL(5, i);
                 tc_fence_after();
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
                     mma_bf16(tm + TP_Y, desc_add(dXh, 2048u * ks), desc_add(dC, kmajor_off(ks)), ID_P_MK, 1u);
                 mma_commit(&bars.g2);
-                HX_TL(6, i);
                 if (i + 1 < n_ch && !(ok = issue_g1(i + 1))) break;
-                HX_TL(7, i);
             }
             if (!ok) atomicCAS(&g_tc_fault, 0u, kFaultMmaOut);
             cb_landed = landed;
@@ -1047,7 +968,6 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             }
         };
         if (lane == 0 && n_ch > 0) mbar_arrive(&bars.v_full[0]);
-        if (lane == 0) HX_TL(21, 0);
         {
             float r[3][2][4];
 #pragma unroll
@@ -1069,7 +989,6 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 warp_load_dt(p, pt.s[1].db, t0 + 3 * kCS, t_end, n1);
             }
             if (i >= kPRing && !(ok = warp_wait(&bars.v_empty[i % kPRing], vpar(i - kPRing)))) break;
-            if (lane == 0) HX_TL(30, i);
             float* vs = slot(i);
 #pragma unroll 1
             for (int v = 0; v < 2; ++v) {
@@ -1087,14 +1006,12 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars.v_full[i % kPRing]);
-            if (lane == 0) HX_TL(21, i);
             if (more) park(i + 3, n0, n1);
             __syncwarp();
         }
     } else if (warp >= kPEpi) {
         // ================= builders: xw = w x, bf16 hi | lo ==================
         const XLane xl = x_lane(p, pt, 32 * bld_index(warp) + lane);
-        const bool lead = warp == 8 && lane == 0;
         uint8_t* xt = sm + OP_XW + 16384u * (uint32_t)xl.sl;  // this slab's hi tile; lo 32 KB on
         uint4 cur[kPV], nxt[kPV];
 #pragma unroll
@@ -1107,11 +1024,9 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             // out, by when it has landed
             if (i + 1 < n_ch) load_x_pair(p, pt, xl, i + 1, nxt);
             if (!(ok = warp_wait(&bars.v_full[i % kPRing], vpar(i)))) break;
-            if (lead) HX_TL(16, i);
             // lo(i-1) was read by G4(i-1) only; before chunk 0, the epilogue
             // reads the span-entry state staged over these buffers
             if (!(ok = i >= 1 ? warp_wait(&bars.g4, (uint32_t)((i - 1) & 1)) : warp_wait(&bars.s_ready, 0u))) break;
-            if (lead) HX_TL(17, i);
             // rows of this thread's vectors: j0 + 12 k; the swizzled 16-byte
             // column depends on the row only through bit 2 (k odd flips it)
             const float* wv = slot(i) + kPSlot * xl.sl + xl.j0;
@@ -1127,10 +1042,8 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                     cur[k] = hi;
                 }
             }
-            if (lead) HX_TL(18, i);
             // hi(i-1) was read by G4(i-1) and G2(i-1)
             if (i >= 1 && !(ok = warp_wait(&bars.g2, (uint32_t)((i - 1) & 1)))) break;
-            if (lead) HX_TL(19, i);
 #pragma unroll
             for (int k = 0; k < kPV; ++k)
                 if (k < kPV - 1 || xl.j0 + kJStep * k < kCS)
@@ -1141,15 +1054,8 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 mbar_arrive(&bars.xw_ready);
                 mbar_arrive(&bars.v_empty[i % kPRing]);
             }
-            if (lead) HX_TL(20, i);
 #pragma unroll
             for (int k = 0; k < kPV; ++k) cur[k] = nxt[k];
-#ifdef HX_PHASE_PROFILE
-            if (lead) {
-                asm volatile("" ::"r"(cur[0].x), "r"(cur[kPV - 2].w));
-                HX_TL(28, i);
-            }
-#endif
         }
     } else {
         // ================= epilogue =========================================
@@ -1243,7 +1149,6 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             // (1) the mask of D1(i), written over C(i) once G3(i) (and G1(i)
             // before it) retired
             if (!(ok = warp_wait(&bars.g3, par))) break;
-            if (tid == 0) HX_TL(9, i);
             tc_fence_after();
             {
                 uint32_t mk[32];
@@ -1255,11 +1160,9 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                         make_uint4(mk[4 * c8], mk[4 * c8 + 1], mk[4 * c8 + 2], mk[4 * c8 + 3]);
                 fence_async_smem();
                 warp_arrive(&bars.m_ready);
-                if (tid == 0) HX_TL(10, i);
             }
             // (2) S_{i+1} from D4 (the last chunk's state is read once y has left)
             if (!(ok = warp_wait(&bars.g4, par))) break;
-            if (tid == 0) HX_TL(11, i);
             const bool last = i + 1 == n_ch;
             if (!last && !(ok = warp_wait(&bars.v_full[(i + 1) % kPRing], vpar(i + 1)))) break;
             tc_fence_after();
@@ -1276,11 +1179,9 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 tmem_wait_st();
                 tc_fence_before();
                 warp_arrive(&bars.s_ready);
-                if (tid == 0) HX_TL(12, i);
             }
             // (3) y(i) = f_t Y
             if (!(ok = warp_wait(&bars.g2, par))) break;
-            if (tid == 0) HX_TL(13, i);
             tc_fence_after();
             {
                 float a[64];
@@ -1289,7 +1190,6 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 tmem_wait_ld();
                 tc_fence_before();
                 warp_arrive(&bars.y_free);
-                if (tid == 0) HX_TL(14, i);
                 const float4* f4 = reinterpret_cast<const float4*>(slot(i) + kPSlot * v + 128 + 64 * kh);
                 const int kmax = tlen - 64 * kh;
                 if (maps.y_ok && (tlen >= kCS || t_end == p.L)) {
@@ -1309,10 +1209,8 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                         yb[(4 * k4 + 2) * 32 + lane] = y2;
                         yb[(4 * k4 + 3) * 32 + lane] = y3;
                     }
-                    if (tid == 0) HX_TL(22, i);
                     fence_async_smem();
                     __syncwarp();
-                    if (tid == 0) HX_TL(23, i);
                     if (lane == 0 && sr.pw > 32 * (q & 1)) {
                         tma_store_4d(&maps.y, yb, sr.p0 + 32 * (q & 1), sr.h, tp + 64 * kh, pt.seq);
                         bulk_commit();
@@ -1335,7 +1233,6 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bars.v_empty[i % kPRing]);
-                if (tid == 0) HX_TL(15, i);
             }
         }
         // every y box written before the CTA ends
@@ -1445,8 +1342,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const PairTile pt = pair_tile(p);
     grid_dep_launch();  // the general-path kernel waits for this grid anyway
-    if (tid == 0) HX_TL(31, 0);
-    if (tid == 0) HX_KS(5);
     if (tid == 0) {
         mbar_init(&cb_bar[0], 1);
         mbar_init(&cb_bar[1], 1);
@@ -1473,13 +1368,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // early: everything above reads only the scan's inputs; the carry
         // kernel's span-entry states are read after the wait
         grid_dep_wait();
-        if (tid == 0) HX_KS(6);
         // the state kernel measured every run's largest chunk decay span
         if (p.run_span && tid == 0) span_bits = tile_span_bits(p, pt);
         load_state_tile(p, pt, st, tid);
-        if (tid == 0) HX_TL(24, 0);
         if (!p.run_span) pair_span(p, pt, warp, kPEpi + kPBld, &span_bits);
-        if (tid == 0) HX_TL(25, 0);
     } else if (warp == kPWarpVec) {
         // the chunk vectors of chunk 0 straight into ring slot 0
         float* vs = reinterpret_cast<float*>(sm + OP_V);
@@ -1496,7 +1388,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
             if (lane == 0) vs[kPSlot * v + 256] = ex2(total);
         }
-        if (lane == 0) HX_TL(26, 0);
     } else if (warp != kPWarpMma) {
         uint4 v[kPV];
         load_x_pair(p, pt, x_lane(p, pt, 32 * bld_index(warp) + lane), 0, v);
@@ -1508,11 +1399,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
             pre[4 * k + 3] = __uint_as_float(v[k].w);
         }
         if (!p.run_span) pair_span(p, pt, kPEpi + bld_index(warp), kPEpi + kPBld, &span_bits);
-        if (warp == 8 && lane == 0) HX_TL(27, 0);
     }
     __syncthreads();
-    if (tid == 0) HX_TL(31, 1);
-    if (tid == 0) HX_KS(7);
     const uint32_t tm = tmem_base;
     const bool fast = pair_takes_fast(p, span_bits, force_general);
     if (tid == 0 && p.tile_flag) p.tile_flag[blockIdx.x] = fast ? 1 : 0;
@@ -1527,7 +1415,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
     out_pair(maps, p, pt, sm, tm, cb_bar, pre);
     tc_fence_before();
     __syncthreads();
-    if (tid == 0) HX_KS(8);
     if (warp == kPWarpMma) {
         tc_fence_after();
         tmem_dealloc(tm, 512);
@@ -1609,9 +1496,7 @@ __global__ void __launch_bounds__(kOutThreads, 1)
 constexpr int kCarryThreads = 256;
 
 __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
-    if (threadIdx.x == 0) HX_KS(2);
     grid_dep_wait();    // the state kernel's run states
-    if (threadIdx.x == 0) HX_KS(3);
     grid_dep_launch();  // the output kernel may start its prologue
     const int64_t per_head4 = (int64_t)p.P * p.N / 4;
     const int64_t gid = (int64_t)blockIdx.x * kCarryThreads + threadIdx.x;
@@ -1620,9 +1505,10 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
     const int e4 = (int)(gid - head_lin * per_head4);
     const int seq = (int)(head_lin / p.H), h = (int)(head_lin % p.H);
     const int c = (4 * e4) / p.N, n = (4 * e4) % p.N;  // N % 4 == 0
-    const int src = p.has_ids ? p.ids[seq] : seq;
+    int src;
+    const bool clear = s0_row(p, seq, &src);
     const float* s0 = p.s0 + (int64_t)src * p.seq_s + (int64_t)h * p.s_s0 + (int64_t)c * p.s_s1 + n;
-    float4 S = make_float4(s0[0], s0[1], s0[2], s0[3]);
+    float4 S = clear ? make_float4(s0[0], s0[1], s0[2], s0[3]) : make_float4(kNaN, kNaN, kNaN, kNaN);
     const int64_t unit0 = head_lin * p.run_slots;
     float4* agg = reinterpret_cast<float4*>(p.agg + unit0 * (int64_t)p.P * p.N) + e4;
     const int R = p.state_runs, K = p.out_k;
@@ -1715,10 +1601,6 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
     __shared__ uint32_t tmem_base;
     __shared__ float lam_total;
 
-    HX_PHASE_START;
-    HX_CTA(0);
-    if (threadIdx.x == 0) HX_TLS(0, 0);
-    if (threadIdx.x == 0) HX_KS(0);
     const int tid = threadIdx.x, warp = tid >> 5;
     const bool is_mma = warp == 8, is_vec = warp == 9;
     const int wg = (warp >> 2) & 1;
@@ -1743,7 +1625,6 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
         warp_load_dt(p, db, t0_of(0), t_end, r0);
         warp_load_dt(p, db, t0_of(min(1, n_ch - 1)), t_end, r1);
         warp_load_dt(p, db, t0_of(min(2, n_ch - 1)), t_end, r2);
-        if ((tid & 31) == 0) HX_TLS(15, 0);
     }
     auto sB = [&](int s) { return sm + SO_B + (uint32_t)(s % kStB) * 16384u; };
     auto sX = [&](int s) { return sm + SO_X + (uint32_t)(s % kStX) * 8192u; };
@@ -1792,16 +1673,10 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
             prefetch_tmap(&maps.x);
             for (int s = 0; s < kStB && s < n_st; ++s) load_b(s);
             for (int s = 0; s < kStX && s < n_st; ++s) load_x(s);
-            HX_PHASE_T(16, 256);
             for (int s = 0; s < n_st && ok; ++s) {
                 const int st = s % kStB;
                 if (!(ok = mbar_wait(&bars.b_full[st], (uint32_t)((s / kStB) & 1), kWaitBudget))) break;
-                if (s == 0 && blockIdx.x < 1024) HX_CTA_T(1);
-                HX_TLS(1, s);
-                HX_PHASE_T(17, 256);
                 if (!(ok = mbar_wait(&bars.xw_full[s % kStXw], (uint32_t)((s / kStXw) & 1), kWaitBudget))) break;
-                HX_TLS(2, s);
-                HX_PHASE_T(18, 256);
                 tc_fence_after();
                 // A = B rows of the step (M = 128 states in two 64-state atoms),
                 // B = [xw_hi | xw_lo] (N = 128 in two atoms), K = 64 tokens
@@ -1812,18 +1687,13 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
                     mma_bf16(tm, desc_add(dA, 2048u * ks), desc_add(dX, 2048u * ks), ID_G4W, (s > 0 || ks > 0) ? 1u : 0u);
                 mma_commit(&bars.xw_empty[s % kStXw]);
                 mma_commit(&bars.b_done[st]);
-                if (s + 1 == n_st) HX_CTA_T(2);
-                HX_TLS(3, s);
-                HX_PHASE_T(19, 256);
                 // the builders consumed x(s) before xw_full
                 if (s + kStX < n_st) load_x(s + kStX);
                 // B(s)'s slot takes B(s + kStB) once this step's MMAs retire
                 if (s + kStB < n_st) {
                     if (!(ok = mbar_wait(&bars.b_done[st], (uint32_t)((s / kStB) & 1), kWaitBudget))) break;
                     load_b(s + kStB);
-                    HX_TLS(4, s);
                 }
-                HX_PHASE_T(20, 256);
             }
             if (!ok) {
                 atomicCAS(&g_tc_fault, 0u, kFaultMmaState);
@@ -1846,7 +1716,6 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
         };
         park(0, r0);
         __syncwarp();
-        if (lane == 0) HX_TLS(10, 0);
 #pragma unroll 1
         for (int q = 0; q < n_ch && ok; ++q) {
             const int t0 = t0_of(q);
@@ -1856,10 +1725,8 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
             const float raw[4] = {dtr[(q & 3) * 128 + 4 * lane], dtr[(q & 3) * 128 + 4 * lane + 1],
                                   dtr[(q & 3) * 128 + 4 * lane + 2], dtr[(q & 3) * 128 + 4 * lane + 3]};
             float v[4], pre[4], total;
-            if (lane == 0) HX_TLS(13, q);
             warp_chunk_prefix(p, db, t0, min(kCS, t_end - t0), Ah2, raw, v, pre, &total);
             span_mx = fmaxf(span_mx, fabsf(total));
-            if (lane == 0) HX_TLS(14, q);
             const int slot = q % kStRing;
             if (q >= kStRing) {
                 if (!(ok = mbar_wait(&bars.w_empty[slot], (uint32_t)(((q - kStRing) / kStRing) & 1), kWaitBudget)))
@@ -1871,7 +1738,6 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
             later += total;
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars.w_full[slot]);
-            if (lane == 0) HX_TLS(9, q);
             if (q == 0) {
                 park(1, r1);
                 park(2, r2);
@@ -1908,22 +1774,16 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
         __syncwarp();
     } else {
         // ---- xw builders: two 16-byte x vectors per thread per step -------
-        HX_PHASE(21);
         for (int s = 0; s < n_st; ++s) {
             const int q = s >> 1, slot = q % kStRing;
             if ((s & 1) == 0) {
                 if (!(ok = st_wait(&bars.w_full[slot], (uint32_t)((q / kStRing) & 1), kFaultMmaState))) break;
             }
-            if (tid == 0) HX_TLS(5, s);
-            HX_PHASE(22);
             if (!(ok = st_wait(&bars.x_full[s % kStX], (uint32_t)((s / kStX) & 1), kFaultTmaState))) break;
-            if (tid == 0) HX_TLS(6, s);
             if (s >= kStXw) {  // xw buffer s % kStXw was last read by step s - kStXw
                 if (!(ok = st_wait(&bars.xw_empty[s % kStXw], (uint32_t)(((s - kStXw) / kStXw) & 1), kFaultMmaState)))
                     break;
             }
-            if (tid == 0) HX_TLS(7, s);
-            HX_PHASE(23);
             const float* wv = wring + slot * 128 + (s & 1) * kStHalf;
             const uint8_t* x = sX(s);
             uint8_t* xh = sXW(s);
@@ -1944,13 +1804,10 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
                 mbar_arrive(&bars.xw_full[s % kStXw]);
                 if (s & 1) mbar_arrive(&bars.w_empty[slot]);
             }
-            if (tid == 0) HX_TLS(8, s);
-            HX_PHASE(25);
         }
         // all G4 MMAs retired: the last step's commit
         if (ok && n_st > 0)
             ok = st_wait(&bars.xw_empty[(n_st - 1) % kStXw], (uint32_t)(((n_st - 1) / kStXw) & 1), kFaultMmaState);
-        if (tid == 0) HX_TLS(11, 0);
         tc_fence_after();
         if (ok) {
             const int64_t unit = ((int64_t)tl.seq * p.H + tl.h) * p.run_slots + tl.run;
@@ -1974,14 +1831,10 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
     __syncthreads();
     if (ok && tid == 0 && tl.slab == 0)
         p.lam[((int64_t)tl.seq * p.H + tl.h) * p.run_slots + tl.run] = lam_total;
-    HX_CTA(3);
-    if (tid == 0) HX_TLS(12, 0);
-    if (tid == 0) HX_KS(1);
     if (is_mma) {
         tc_fence_after();
         tmem_dealloc(tm, 128);
     }
-    HX_PHASE(26);
 }
 
 // ---------------------------------------------------------------------------
@@ -2119,6 +1972,13 @@ int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, 
     tc_state_kernel<<<(unsigned)(per_run * pl.state_runs), kStThreads, SMEM_STATE, static_cast<cudaStream_t>(stream)>>>(
         maps, p, pl.state_runs);
     return cudaGetLastError();
+}
+
+int fault_word_address(unsigned** out) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_tc_fault);
+    *out = static_cast<unsigned*>(ptr);
+    return e;
 }
 
 int read_tc_fault(unsigned* code) {

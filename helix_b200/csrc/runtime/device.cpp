@@ -15,16 +15,28 @@
 namespace hx {
 
 namespace {
-// Keyed by context so two contexts used from one thread keep separate
-// messages; thread_local so concurrent encoders never race on it.
-thread_local std::map<const helix_ctx*, std::string> t_errors;
+// Errors raised before a context exists (helix_ctx_create), per thread.
+thread_local std::string t_null_error;
 }  // namespace
 
-void set_error(const helix_ctx* ctx, const std::string& msg) { t_errors[ctx] = msg; }
+void set_error(const helix_ctx* ctx, const std::string& msg) {
+    if (!ctx) {
+        t_null_error = msg;
+        return;
+    }
+    auto* c = const_cast<helix_ctx*>(ctx);
+    std::lock_guard<std::mutex> lk(c->err_mu);
+    c->errors[std::this_thread::get_id()] = msg;
+}
 
+// The string stays valid until this thread's next error on ctx, or until
+// ctx is freed.
 const char* get_error(const helix_ctx* ctx) {
-    auto it = t_errors.find(ctx);
-    return it == t_errors.end() ? "" : it->second.c_str();
+    if (!ctx) return t_null_error.c_str();
+    auto* c = const_cast<helix_ctx*>(ctx);
+    std::lock_guard<std::mutex> lk(c->err_mu);
+    auto it = c->errors.find(std::this_thread::get_id());
+    return it == c->errors.end() ? "" : it->second.c_str();
 }
 
 }  // namespace hx
@@ -94,6 +106,10 @@ extern "C" helix_status helix_ctx_create(helix_ctx** out, void* device, const ch
         }
         ctx->tc_ready = hx::configure_tc(ctx) == cudaSuccess;
         if (!ctx->tc_ready) cudaGetLastError();
+        if (hx::fault_word_address(&ctx->fault_word) != cudaSuccess) {
+            cudaGetLastError();
+            ctx->fault_word = nullptr;
+        }
 
         cudaDriverEntryPointQueryResult q{};
         void* fn = nullptr;

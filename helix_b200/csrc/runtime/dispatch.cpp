@@ -19,36 +19,41 @@ T* at(helix_tensor t) {
     return reinterpret_cast<T*>(static_cast<char*>(t.buf) + t.offset);
 }
 
-// Byte extent [lo, hi) touched by a state tensor of this descriptor.
-void state_extent(const helix_scan_desc& d, helix_tensor t, int64_t n_rows, uintptr_t* lo,
-                  uintptr_t* hi) {
+// Byte extent [lo, hi) touched by n_rows rows of a state tensor of d.
+void state_extent(const helix_scan_desc& d, const void* base, int64_t n_rows, uintptr_t* lo, uintptr_t* hi) {
     const int64_t last = (n_rows - 1) * d.seq_s + (int64_t)(d.n_head - 1) * d.s_s[0] +
                          (int64_t)(d.head_dim - 1) * d.s_s[1] + (int64_t)(d.d_state - 1);
-    *lo = reinterpret_cast<uintptr_t>(at<char>(t));
+    *lo = reinterpret_cast<uintptr_t>(base);
     *hi = *lo + (uintptr_t)(last + 1) * sizeof(float);
 }
 
-// Best-effort size check of the caller's scratch: when the driver knows the
-// allocation containing it, the plan must fit inside that allocation.
-bool scratch_fits(helix_tensor s, size_t need) {
-    using range_fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+using range_fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+range_fn address_range_fn() {
     static range_fn fn = [] {
         void* f = nullptr;
         cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) !=
-                cudaSuccess ||
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
             q != cudaDriverEntryPointSuccess) {
             cudaGetLastError();
             return (range_fn) nullptr;
         }
         return reinterpret_cast<range_fn>(f);
     }();
-    if (!fn) return true;
-    CUdeviceptr base = 0;
+    return fn;
+}
+
+// [base, end) of the driver allocation holding p; false when the driver does
+// not know p (host memory, or no driver entry point).
+bool allocation_of(const void* p, uintptr_t* base, uintptr_t* end) {
+    const range_fn fn = address_range_fn();
+    if (!fn) return false;
+    CUdeviceptr b = 0;
     size_t size = 0;
-    const CUdeviceptr p = reinterpret_cast<CUdeviceptr>(at<char>(s));
-    if (fn(&base, &size, p) != CUDA_SUCCESS) return true;  // unknown: cannot check
-    return p + need <= base + size;
+    if (fn(&b, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return false;
+    *base = (uintptr_t)b;
+    *end = (uintptr_t)b + size;
+    return true;
 }
 
 helix_status encode_core(helix_ctx* ctx, void* stream, const helix_scan_desc* d, helix_tensor s0,
@@ -65,7 +70,6 @@ helix_status encode_core(helix_ctx* ctx, void* stream, const helix_scan_desc* d,
         hx::set_error(ctx, why);
         return HELIX_ERR_UNSUPPORTED_SHAPE;
     }
-
     const hx::Plan pl = hx::make_plan(ctx, *d);
     if (pl.total > 0) {
         if (!scratch.buf) {
@@ -76,68 +80,96 @@ helix_status encode_core(helix_ctx* ctx, void* stream, const helix_scan_desc* d,
             hx::set_error(ctx, "scratch must be 256-byte aligned");
             return HELIX_ERR_INVALID_ARG;
         }
-        if (!scratch_fits(scratch, pl.total)) {
+        if (!hx::scratch_fits(at<char>(scratch), pl.total)) {
             hx::set_error(ctx, "scratch allocation smaller than helix_scan_scratch_size()");
             return HELIX_ERR_SCRATCH_TOO_SMALL;
         }
     }
-
-    // s0 is read while s1 is written by other CTAs of the same launch.
-    {
-        uintptr_t a0, a1, b0, b1;
-        int64_t src_rows = d->n_seq;
-        state_extent(*d, s0, src_rows, &a0, &a1);
-        state_extent(*d, s1, d->n_seq, &b0, &b1);
-        if (a0 < b1 && b0 < a1) {
-            hx::set_error(ctx, "s0 and s1 overlap");
-            return HELIX_ERR_INVALID_ARG;
-        }
-    }
-
     hx::ScanParams p{};
-    hx::fill_params(p, *d, pl);
-    p.has_ids = ids.buf ? 1 : 0;
-    p.x = at<void>(x);
-    p.dt = at<float>(dt);
-    p.A = at<float>(A);
-    p.B = at<void>(B);
-    p.C = at<void>(C);
-    p.ids = ids.buf ? at<int32_t>(ids) : nullptr;
-    p.s0 = at<float>(s0);
-    p.y = at<float>(y);
-    p.s1 = at<float>(s1);
-    if (pl.total > 0) {
-        p.agg = reinterpret_cast<float*>(at<char>(scratch) + pl.off_agg);
-        p.lam = reinterpret_cast<float*>(at<char>(scratch) + pl.off_lam);
-        p.tile_flag = pl.has_flags ? reinterpret_cast<int32_t*>(at<char>(scratch) + pl.off_flag) : nullptr;
-        p.run_span = pl.has_span ? reinterpret_cast<float*>(at<char>(scratch) + pl.off_span) : nullptr;
-    }
+    const hx::CallTensors t{s0, x, dt, A, B, C, ids, y, s1};
+    const helix_status st = hx::bind_call(ctx, *d, pl, t, &p);
+    if (st != HELIX_OK) return st;
+    if (pl.total > 0) hx::bind_scratch(pl, at<char>(scratch), &p);
+    return hx::run_call(ctx, pl, p, stream);
+}
 
-    if (pl.path == hx::kPathTcBf16) {
+}  // namespace
+
+namespace hx {
+
+bool scratch_fits(const void* s, size_t need) {
+    uintptr_t base = 0, end = 0;
+    if (!allocation_of(s, &base, &end)) return true;  // unknown: cannot check
+    return reinterpret_cast<uintptr_t>(s) + need <= end;
+}
+
+bool states_overlap(const helix_scan_desc& d, const void* s0, const void* s1) {
+    uintptr_t a0, a1, b0, b1;
+    state_extent(d, s0, d.n_seq, &a0, &a1);
+    state_extent(d, s1, d.n_seq, &b0, &b1);
+    return a0 < b1 && b0 < a1;
+}
+
+helix_status bind_call(helix_ctx* ctx, const helix_scan_desc& d, const Plan& pl, const CallTensors& t,
+                       ScanParams* out) {
+    if (!t.s0.buf || !t.x.buf || !t.dt.buf || !t.A.buf || !t.B.buf || !t.C.buf || !t.y.buf || !t.s1.buf) {
+        set_error(ctx, "null tensor");
+        return HELIX_ERR_INVALID_ARG;
+    }
+    // s0 is read while s1 is written by other CTAs of the same launch.  Rows
+    // that only ids reaches are checked by the kernels that read them
+    // (kFaultIdsOverlap: that sequence comes out NaN).
+    if (states_overlap(d, at<char>(t.s0), at<char>(t.s1))) {
+        set_error(ctx, "s0 and s1 overlap");
+        return HELIX_ERR_INVALID_ARG;
+    }
+    ScanParams& p = *out;
+    p = ScanParams{};
+    fill_params(p, d, pl);
+    p.has_ids = t.ids.buf ? 1 : 0;
+    p.x = at<void>(t.x);
+    p.dt = at<float>(t.dt);
+    p.A = at<float>(t.A);
+    p.B = at<void>(t.B);
+    p.C = at<void>(t.C);
+    p.ids = t.ids.buf ? at<int32_t>(t.ids) : nullptr;
+    p.s0 = at<float>(t.s0);
+    p.y = at<float>(t.y);
+    p.s1 = at<float>(t.s1);
+    p.fault = ctx->fault_word;
+    if (pl.path == kPathTcBf16) {
         // TMA needs 16-byte aligned global bases.
         const uintptr_t m = reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.B) |
                             reinterpret_cast<uintptr_t>(p.C);
         if (m & 15) {
-            hx::set_error(ctx, "x, B and C must be 16-byte aligned for the tensor-core path");
+            set_error(ctx, "x, B and C must be 16-byte aligned for the tensor-core path");
             return HELIX_ERR_UNSUPPORTED_SHAPE;
         }
     }
+    return HELIX_OK;
+}
 
+void bind_scratch(const Plan& pl, char* base, ScanParams* p) {
+    p->agg = reinterpret_cast<float*>(base + pl.off_agg);
+    p->lam = reinterpret_cast<float*>(base + pl.off_lam);
+    p->tile_flag = pl.has_flags ? reinterpret_cast<int32_t*>(base + pl.off_flag) : nullptr;
+    p->run_span = pl.has_span ? reinterpret_cast<float*>(base + pl.off_span) : nullptr;
+}
+
+helix_status run_call(helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream) {
     int dev_prev = -1;
     cudaGetDevice(&dev_prev);
     if (dev_prev != ctx->device) cudaSetDevice(ctx->device);
-    const int rc = pl.path == hx::kPathTcBf16 ? hx::launch_tc(ctx, pl, p, stream)
-                                               : hx::launch_simt(ctx, pl, p, stream);
+    const int rc = pl.path == kPathTcBf16 ? launch_tc(ctx, pl, p, stream) : launch_simt(ctx, pl, p, stream);
     if (dev_prev >= 0 && dev_prev != ctx->device) cudaSetDevice(dev_prev);
     if (rc != cudaSuccess) {
-        hx::set_error(ctx, std::string("kernel launch failed: ") +
-                               cudaGetErrorString(static_cast<cudaError_t>(rc)));
+        set_error(ctx, std::string("kernel launch failed: ") + cudaGetErrorString(static_cast<cudaError_t>(rc)));
         return HELIX_ERR_PIPELINE;
     }
     return HELIX_OK;
 }
 
-}  // namespace
+}  // namespace hx
 
 namespace hx {
 
@@ -170,6 +202,9 @@ void fill_params(ScanParams& p, const helix_scan_desc& d, const Plan& pl) {
     p.s_s0 = d.s_s[0]; p.s_s1 = d.s_s[1]; p.seq_s = d.seq_s;
     p.s_y0 = d.s_y[0]; p.s_y1 = d.s_y[1]; p.s_y2 = d.s_y[2]; p.seq_y = d.seq_y;
     p.s_a = d.s_a;
+    const int64_t row = (int64_t)(d.n_head - 1) * d.s_s[0] + (int64_t)(d.head_dim - 1) * d.s_s[1] + d.d_state;
+    p.s_row_bytes = row * (int64_t)sizeof(float);
+    p.s1_bytes = ((int64_t)(d.n_seq - 1) * d.seq_s + row) * (int64_t)sizeof(float);
 }
 
 }  // namespace hx

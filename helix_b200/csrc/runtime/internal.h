@@ -17,7 +17,10 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <map>
+#include <mutex>
 #include <string>
+#include <thread>
 
 #include "helix/helix.h"
 
@@ -98,17 +101,27 @@ struct ScanParams {
     float*         lam;
     int32_t*       tile_flag;  // scratch or null, see Plan
     float*         run_span;   // scratch or null, see Plan
+
+    unsigned*      fault;       // the device fault word (helix_device_fault)
+    int64_t        s_row_bytes; // bytes one s0 / s1 row spans
+    int64_t        s1_bytes;    // bytes the n_seq rows of s1 span
 };
 
 }  // namespace hx
 
 struct helix_ctx {
+    // Last error per calling thread (helix_ctx_last_error); freed with the
+    // context.  Only error paths touch it.
+    std::mutex err_mu;
+    std::map<std::thread::id, std::string> errors;
+
     int    device      = 0;
     int    n_sm        = 0;
     int    cc_major    = 0;
     int    cc_minor    = 0;
     size_t max_smem_optin = 0;
     bool   tc_ready    = false;   // tensor-core kernels configured
+    unsigned* fault_word = nullptr; // device address of the fault word
     void*  encode_tiled = nullptr; // cuTensorMapEncodeTiled entry point
 };
 
@@ -129,6 +142,27 @@ Path select_path(const helix_scan_desc& d);
 // dispatch.cpp: fills everything but the tensor pointers.
 void fill_params(ScanParams& p, const helix_scan_desc& d, const Plan& pl);
 
+// The tensors of one scan call, as the caller passed them.
+struct CallTensors {
+    helix_tensor s0, x, dt, A, B, C, ids, y, s1;
+};
+// Checks the call's tensors (none null, s1 clear of every s0 row the call
+// may read, TMA alignment on the tensor-core path) and fills *p from d, the
+// plan and the tensors; scratch pointers are left null.  Shared by every
+// entry point that runs a scan, so each check exists once.
+helix_status bind_call(helix_ctx* ctx, const helix_scan_desc& d, const Plan& pl, const CallTensors& t,
+                       ScanParams* p);
+// Points the plan's scratch regions of *p into base.
+void bind_scratch(const Plan& pl, char* base, ScanParams* p);
+// Enqueues the plan's kernels on stream, on ctx's device.
+helix_status run_call(helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+// Whether the driver allocation holding s has need bytes from s on (true
+// when the driver does not know s: a raw pointer carries no length).
+bool scratch_fits(const void* s, size_t need);
+// Whether the n_seq rows of s1 overlap the first n_seq rows of s0.  (Rows
+// that only ids reaches are checked on the device; see s0_row.)
+bool states_overlap(const helix_scan_desc& d, const void* s0, const void* s1);
+
 // Kernel launchers (kernels/*.cu).  Return cudaSuccess or the launch error.
 int launch_simt(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
@@ -148,5 +182,7 @@ int launch_carry_combine(const ScanParams& p, const float* states, const float* 
 int configure_simt(const helix_ctx* ctx);
 int configure_tc(const helix_ctx* ctx);
 int read_tc_fault(unsigned* code);
+// Device address of the fault word on the current device.
+int fault_word_address(unsigned** out);
 
 }  // namespace hx

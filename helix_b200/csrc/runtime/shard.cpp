@@ -71,6 +71,10 @@ extern "C" helix_status helix_scan_shard_state(helix_ctx* ctx, void* stream, con
         hx::set_error(ctx, "scratch must be 256-byte aligned");
         return HELIX_ERR_INVALID_ARG;
     }
+    if (!hx::scratch_fits(at<char>(scratch), pl.total)) {
+        hx::set_error(ctx, "scratch allocation smaller than helix_scan_shard_state_scratch_size()");
+        return HELIX_ERR_SCRATCH_TOO_SMALL;
+    }
     hx::ScanParams p{};
     hx::fill_params(p, m, pl);
     p.x = at<void>(x);
@@ -108,16 +112,9 @@ extern "C" helix_status helix_scan_carry_combine(helix_ctx* ctx, void* stream, c
         hx::set_error(ctx, "bad state shape or innermost state stride != 1");
         return HELIX_ERR_UNSUPPORTED_SHAPE;
     }
-    {
-        const int64_t last = (int64_t)(d->n_seq - 1) * d->seq_s + (int64_t)(d->n_head - 1) * d->s_s[0] +
-                             (int64_t)(d->head_dim - 1) * d->s_s[1] + (int64_t)(d->d_state - 1);
-        const uintptr_t a0 = reinterpret_cast<uintptr_t>(at<char>(s0));
-        const uintptr_t b0 = reinterpret_cast<uintptr_t>(at<char>(carry));
-        const uintptr_t span = (uintptr_t)(last + 1) * sizeof(float);
-        if (a0 < b0 + span && b0 < a0 + span) {
-            hx::set_error(ctx, "s0 and carry overlap");
-            return HELIX_ERR_INVALID_ARG;
-        }
+    if (hx::states_overlap(*d, at<char>(s0), at<char>(carry))) {
+        hx::set_error(ctx, "s0 and carry overlap");
+        return HELIX_ERR_INVALID_ARG;
     }
     hx::Plan pl{};
     hx::ScanParams p{};
@@ -125,6 +122,8 @@ extern "C" helix_status helix_scan_carry_combine(helix_ctx* ctx, void* stream, c
     p.has_ids = ids.buf ? 1 : 0;
     p.ids = ids.buf ? at<int32_t>(ids) : nullptr;
     p.s0 = at<float>(s0);
+    p.s1 = at<float>(carry);  // the rows written, for the device-side ids check
+    p.fault = ctx->fault_word;
     DeviceScope ds(ctx->device);
     const int rc = hx::launch_carry_combine(p, n_prev ? at<float>(states) : nullptr,
                                             n_prev ? at<float>(log_decays) : nullptr, (int)n_prev,

@@ -25,13 +25,15 @@ helix_status helix_device_fault(helix_ctx* ctx, uint32_t* code);
  * workspace, plugins inside a process that owns all device memory, code that
  * may not allocate after start-up).  Same arguments and results as
  * helix_scan_encode with multipass forced on, minus `scratch`: the run
- * scratch lives in a 32 MiB array inside the library, present on every GPU
- * that loads the library until the process exits.
+ * scratch lives in a 32 MiB array inside the library.
+ *   - The first call on a device loads the array (CUDA reserves its 32 MiB
+ *     then, with lazy module loading) and the device keeps it until the
+ *     process exits.  Make that first call at start-up, before any stream
+ *     capture; if the device has no room for the array the call fails with
+ *     HELIX_ERR_PIPELINE and nothing is enqueued.
  *   - Descriptors needing more than 32 MiB of run scratch are rejected with
  *     HELIX_ERR_SCRATCH_TOO_SMALL (message in helix_ctx_last_error);
  *     nothing is enqueued.
- *   - The first call on a device looks up the array's address
- *     (cudaGetSymbolAddress); make that first call before any stream capture.
  *   - All calls on a device share the array: calls that can overlap on the
  *     GPU race and must be serialised by the caller.  Nothing in it needs to
  *     start at zero (each call writes what it later reads).

@@ -10,6 +10,7 @@ ScanDesc.  Nothing here is used by the shipped library.
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from pathlib import Path
 
@@ -26,9 +27,15 @@ _I = C.POINTER(C.c_int32)
 _D = C.POINTER(C.c_double)
 
 
+# Where the reference checkout is mounted in the build container; the GPU box
+# has no reference and uses the prebuilt oracle/_ref.  HELIX_REF_ROOT overrides.
+REF_MOUNT = "/root/reference"
+
+
 def build() -> None:
     """Runs oracle/Makefile (builds _ref too when the reference sources exist)."""
-    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    ref = os.environ.get("HELIX_REF_ROOT", REF_MOUNT)
+    subprocess.run(["make", "-s", "-C", str(HERE), f"REF_ROOT={ref}"], check=True)
 
 
 def _f(a):

@@ -174,51 +174,6 @@ __global__ void __launch_bounds__(128, 1) probe_kernel(int mode, const __grid_co
     if (warp == 0) tmem_dealloc(tm, 256);
 }
 
-// Timing: `reps` back-to-back MMAs of one configuration on fixed smem
-// operands (all K steps alias the same 16-element slice), accumulating into
-// TMEM; thread 0 records the cycles from first issue to completion.
-// Operand footprints: A at [0, 32 KB), B at [32 KB, 96 KB).  An MN-major
-// operand spans N/64 atoms at a 8 KB stride (at most 4 x 8 KB + 2 KB rows),
-// a K-major one N rows of 128 B (at most 32 KB); both stay inside the
-// 96 KB + 1 KB allocation.
-__global__ void __launch_bounds__(128, 1) mma_rate_kernel(int a_mn, int b_mn, int n, int reps,
-                                                          long long* cycles, unsigned* status) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t bar;
-    __shared__ uint32_t tmem_base;
-    const int tid = threadIdx.x, warp = tid >> 5;
-    for (int i = tid; i < 98304 / 16; i += 128) reinterpret_cast<uint4*>(sm)[i] = make_uint4(0, 0, 0, 0);
-    if (tid == 0) {
-        mbar_init(&bar, 1);
-        fence_mbar_init();
-    }
-    if (warp == 0) {
-        tmem_alloc(&tmem_base, 256);
-        tmem_relinquish();
-    }
-    fence_async_smem();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tm = tmem_base;
-    if (tid == 0) {
-        const uint32_t a = smem_u32(sm), b = smem_u32(sm + 32768);
-        const uint64_t ad = a_mn ? sdesc_sw128(a, 8192, 1024) : sdesc_sw128(a, 16, 1024);
-        const uint64_t bd = b_mn ? sdesc_sw128(b, 8192, 1024) : sdesc_sw128(b, 16, 1024);
-        const uint32_t id = idesc_bf16(128, n, a_mn != 0, b_mn != 0);
-        const long long t0 = clock64();
-        for (int r = 0; r < reps; ++r) mma_bf16(tm, ad, bd, id, r > 0);
-        mma_commit(&bar);
-        const bool ok = mbar_wait(&bar, 0, 1ll << 31);
-        const long long t1 = clock64();
-        *cycles = t1 - t0;
-        if (!ok) *status = 1;
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) tmem_dealloc(tm, 256);
-}
-
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -253,17 +208,6 @@ extern "C" int umma_probe(int mode, const void* P, const void* Q, float* D, unsi
     cudaFuncSetAttribute(probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     probe_kernel<<<1, 128, smem>>>(mode, maps, static_cast<const __nv_bfloat16*>(P),
                                    static_cast<const __nv_bfloat16*>(Q), D, status);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return (int)e;
-    return (int)cudaDeviceSynchronize();
-}
-
-// Cycles for `reps` MMAs of shape 128 x n x 16 (bf16), A/B K- or MN-major.
-extern "C" int umma_rate(int a_mn, int b_mn, int n, int reps, long long* cycles_dev, unsigned* status) {
-    if (n < 8 || n > 256 || n % 16 != 0) return -1;
-    const int smem = 98304 + 1024;
-    cudaFuncSetAttribute(mma_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    mma_rate_kernel<<<1, 128, smem>>>(a_mn, b_mn, n, reps, cycles_dev, status);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
     return (int)cudaDeviceSynchronize();

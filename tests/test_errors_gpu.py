@@ -102,6 +102,82 @@ def test_overlapping_states(ctx, cuda):
     assert "overlap" in ctx.last_error()
 
 
+def _fault(ctx):
+    code = C.c_uint32(0)
+    assert ctx.lib.helix_device_fault(ctx.handle, C.byref(code)) == abi.HELIX_OK
+    return code.value
+
+
+@pytest.mark.parametrize("compute,multipass", [("f32", False), ("f32", True), ("bf16", False), ("bf16", True)])
+def test_ids_row_overlapping_s1(ctx, cuda, compute, multipass):
+    """ids may select any row of s0, beyond the n_seq rows the host can check.
+    A selected row that overlaps the s1 rows being written is not read: that
+    sequence comes out NaN and the fault word records code 5; a row clear of
+    s1 in the same allocation runs normally."""
+    t = _problem(cuda, L=300, H=2)
+    S, H, P, N = t["s0"].shape
+    buf = torch.randn(4, S, H, P, N, device=cuda) * 0.1  # rows 0..3 of one allocation
+    s1 = buf[2]
+    io = torch.bfloat16 if compute == "bf16" else torch.float32
+    x, B, Cm = t["x"].to(io), t["B"].to(io), t["C"].to(io)
+    d = helix_b200.desc_from_tensors(x, t["dt"], B, buf[0], t["y"], multipass=multipass, compute=compute)
+    n = ctx.scratch_size(d)
+    scratch = torch.empty(max(n, 256), dtype=torch.uint8, device=cuda) if n else None
+    _fault(ctx)  # clear
+    for row, bad in ((2, True), (3, False)):
+        ids = torch.tensor([row], dtype=torch.int32, device=cuda)
+        t["y"].fill_(0.0)
+        s1.fill_(0.0)
+        st = ctx.encode(d, buf[0], x, t["dt"], t["A"], B, Cm, t["y"], s1, ids=ids, scratch=scratch)
+        assert st == abi.HELIX_OK, ctx.last_error()
+        torch.cuda.synchronize()
+        code = _fault(ctx)
+        if bad:
+            assert code == 5, code
+            assert bool(torch.isnan(t["y"]).all()) and bool(torch.isnan(s1).all())
+        else:
+            assert code == 0, code
+            assert bool(torch.isfinite(t["y"]).all()) and bool(torch.isfinite(s1).all())
+
+
+def test_carry_combine_ids_row_overlapping_carry(ctx, cuda):
+    S, H, P, N = 1, 2, 64, 128
+    buf = torch.randn(4, S, H, P, N, device=cuda)
+    x = torch.empty(S, 128, H, P, device=cuda)
+    dt = torch.empty(S, 128, H, device=cuda)
+    Bm = torch.empty(S, 128, 1, N, device=cuda)
+    d = helix_b200.desc_from_tensors(x, dt, Bm, buf[0], multipass=True)
+    _fault(ctx)
+    for row, bad in ((1, True), (3, False)):
+        ids = torch.tensor([row], dtype=torch.int32, device=cuda)
+        carry = buf[1]
+        st = ctx.encode_carry_combine(d, buf[0], buf[:0], torch.empty(0, device=cuda), 0, carry, ids=ids)
+        assert st == abi.HELIX_OK, ctx.last_error()
+        torch.cuda.synchronize()
+        assert _fault(ctx) == (5 if bad else 0)
+        assert bool(torch.isnan(carry).all()) == bad
+
+
+def test_error_strings_per_thread_and_freed_with_context(cuda):
+    import threading
+    t = _problem(cuda)
+    a = helix_b200.Context(0)
+    d = _desc(t, multipass=False)
+    d.a_form = abi.HELIX_A_DIAG_PER_CHANNEL
+    assert not a.supported(d)
+    assert "diagonal" in a.last_error()
+    seen = {}
+    th = threading.Thread(target=lambda: seen.setdefault("other", a.last_error()))
+    th.start()
+    th.join()
+    assert seen["other"] == ""  # another thread has no error on this context
+    a.close()
+    for _ in range(8):  # later contexts start clean, wherever they are allocated
+        b = helix_b200.Context(0)
+        assert b.last_error() == ""
+        b.close()
+
+
 def test_encode_into_same_as_encode(ctx, cuda):
     t = _problem(cuda)
     d = _desc(t, multipass=False)

@@ -19,6 +19,7 @@ import pytest
 
 from gpu_harness import BF16_ABS, BF16_REL, BF16_RL2, F32_ABS, F32_REL, F32_RL2, record, widen
 from helpers import compare
+from helix_b200 import abi
 
 pytestmark = pytest.mark.gpu
 
@@ -187,3 +188,37 @@ def test_lsplit_two_ranks_nccl(oracle, tmp_path):
     y = np.concatenate([np.load(tmp_path / f"y{r}.npy") for r in range(world)], axis=1)
     _check("lsplit nccl y", y, y_ref, Y_BOUNDS["bf16"])
     _check("lsplit nccl s1", np.load(tmp_path / f"s{world - 1}.npy"), s_ref, ST_BOUNDS["bf16"])
+
+
+def test_shard_state_rejects_small_scratch(ctx):
+    """A scratch allocation smaller than helix_scan_shard_state_scratch_size()
+    is rejected (the driver knows the allocation's size) and nothing runs."""
+    import ctypes as C
+
+    import helix_b200
+    import torch
+    dev = torch.device("cuda:0")
+    S, L, H, P, N, G = 1, 1024, 4, 64, 128, 1
+    x = torch.randn(S, L, H, P, device=dev)
+    dt = torch.randn(S, L, H, device=dev) - 4
+    A = -torch.rand(H, device=dev) - 1
+    Bm = torch.randn(S, L, G, N, device=dev) / 11
+    Cm = torch.randn(S, L, G, N, device=dev) / 11
+    state = torch.full((S, H, P, N), float("nan"), device=dev)
+    ld = torch.full((S, H), float("nan"), device=dev)
+    d = helix_b200.desc_from_tensors(x, dt, Bm, state, multipass=True)
+    need = ctx.shard_state_scratch_size(d)
+    assert need > 4096
+    rt = C.CDLL("libcudart.so.12")
+    ptr = C.c_void_p()
+    assert rt.cudaMalloc(C.byref(ptr), C.c_size_t(need - 4096)) == 0
+    try:
+        T = helix_b200._t
+        st = ctx.lib.helix_scan_shard_state(ctx.handle, None, C.byref(d), T(x), T(dt), T(A), T(Bm), T(Cm),
+                                            T(state), T(ld), abi.Tensor(ptr, 0))
+        assert st == abi.HELIX_ERR_SCRATCH_TOO_SMALL
+        assert "scratch" in ctx.last_error()
+    finally:
+        torch.cuda.synchronize()
+        rt.cudaFree(ptr)
+    assert bool(torch.isnan(state).all()) and bool(torch.isnan(ld).all())

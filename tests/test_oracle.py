@@ -3,7 +3,7 @@
 1. Golden vectors (tests/golden/*.npz) hold y, s1 and boundary states that the
    REFERENCE's own fp64 oracle produced; the restated input generator must
    reproduce the recorded inputs (checksum) and the restatement must reproduce
-   the outputs.  These run anywhere (no /root/reference needed).
+   the outputs.  These run anywhere (no reference checkout needed).
 2. Where the reference oracle is built here (oracle/_ref), the restatement is
    compared with it directly on the reference's shape matrix
    (reference tests/test_algebra.cpp:28-44) in both memory regimes.

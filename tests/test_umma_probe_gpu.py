@@ -32,24 +32,3 @@ def test_umma_layout(probe, cuda, mode):
     want = {0: Pf @ Qf.T, 1: Pf @ Qf.T, 2: Pf @ Qf[:, :64], 3: Pf.T @ Qf[:, :64], 4: Pf @ Qf.T}[mode]
     err = (D - want).abs().max().item()
     assert err <= 1e-3 * want.abs().max().item(), (mode, err)
-
-
-RATES = [(0, 0, 128), (0, 0, 256), (0, 1, 64), (0, 1, 128), (0, 1, 256), (1, 1, 64), (1, 1, 128), (1, 1, 256)]
-
-
-@pytest.mark.parametrize("cfg", RATES, ids=[f"A{'MN' if a else 'K'}_B{'MN' if b else 'K'}_N{n}" for a, b, n in RATES])
-def test_umma_rate(probe, cuda, cfg):
-    """Issue-to-completion cycles of 512 back-to-back 128xNx16 bf16 MMAs
-    (recorded with HELIX_TEST_STATS; asserts only that they complete)."""
-    from gpu_harness import record
-    a_mn, b_mn, n = cfg
-    probe.umma_rate.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
-    cyc = torch.zeros(1, dtype=torch.int64, device=cuda)
-    status = torch.zeros(1, dtype=torch.int32, device=cuda)
-    assert probe.umma_rate(a_mn, b_mn, n, 512, cyc.data_ptr(), status.data_ptr()) == 0
-    assert int(status.item()) == 0
-    per = cyc.item() / 512
-    flop_per_cycle = 2 * 128 * n * 16 / per
-    record(f"umma rate A{'MN' if a_mn else 'K'} B{'MN' if b_mn else 'K'} N{n}", cycles_per_mma=per,
-           flop_per_cycle=flop_per_cycle)
-    assert per > 0
