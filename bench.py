@@ -1,27 +1,32 @@
 """Benchmark of the SSD prefill scan (one JSON line on rank 0).
 
-Workload: per rank, S=1, L=8192, H=64, P=64, N=128, G=8,
-x/B/C bf16, dt/A/s0 f32, y/s1 f32, multipass.  Under torchrun each rank owns
-its own block of 64 heads of a head-sharded layer (no collective on the data
-path: "scaling": "weak"); `value` counts C3-equivalent tokens, i.e. tokens x
-(heads processed / 64), summed over ranks, over the max device time of any
-rank.
+Workload: S=1, L=8192, H=64, P=64, N=128, G=8, x/B/C
+bf16, dt/A/s0 f32, y/s1 f32, multipass.  Under torchrun the 64 heads of that
+one problem are split over the ranks in whole head groups (8 heads per rank
+at N=8); heads never interact, so there is no collective on the data path
+("scaling": "strong").  `value` = the problem's tokens over the max device
+time of any rank.  --scaling weak gives every rank its own 64-head block
+instead (value counts tokens x heads / 64, summed over ranks).
 
 Timing: W warm-up steps, then K steps; before each step a 256 MiB buffer is
 written (flushing the 126 MB L2; the flush is outside the timed events); each
 step is bracketed by CUDA events on the launching stream; barrier +
 synchronize on both sides of the loop; max over ranks.
 
-Also reported: per-kernel attribution and roofline (the output kernel is the
-dominant one), e2e through the C ABI with pinned host buffers (H2D of the
-step's inputs and D2H of y and s1 inside the timed region; steps in flight on
-two buffer sets with the copies on their own streams, the one-step-at-a-time
-figure beside it as serial_ms_per_step), the CPU baseline
-(the reference's own fp64 oracle, compiled from its sources into oracle/_ref,
-run over (seq, head) slices on all host cores, on a bounded sample), and SM
-clocks sampled during the timed region.
+Also reported: per-pass attribution (state, carry and output passes timed
+alone, each with its algorithmic bytes, GB/s and fraction of measured HBM
+bandwidth, and the state pass's contraction rate), the roofline of the
+output kernel (the dominant one), e2e through the C ABI with pinned host
+buffers (H2D of the step's inputs and D2H of y and s1 inside the timed region;
+steps in flight on two buffer sets with the copies on their own streams, the
+one-step-at-a-time figure beside it as serial_ms_per_step), the CPU baselines
+(the reference's own fp64 oracles -- sequential scan and chunked scan --
+compiled from its sources into oracle/_ref, run over (seq, head) slices on
+all host cores over the whole workload), and SM clocks sampled during the
+timed region.
 
---impl reference times the reference's CPU implementation alone (rank 0).
+--impl reference times the reference's CPU implementation alone (rank 0): one
+step is one whole scan of the workload.
 """
 from __future__ import annotations
 
@@ -50,7 +55,12 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c3")
     ap.add_argument("--compute", default="bf16", choices=["bf16", "f32"])
-    ap.add_argument("--cpu-sample-tokens", type=int, default=2048)
+    ap.add_argument("--io", default="config", choices=["config", "bf16", "f32"],
+                    help="storage of x, B, C (default: the config's)")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="N>1: split one problem's heads over the ranks (strong) or give each rank its own")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=0,
+                    help="tokens of the CPU baseline's sample (0: the whole sequence)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--lsplit", type=int, default=0,
@@ -62,7 +72,10 @@ def parse():
 # ---------------------------------------------------------------------------
 # CPU baseline: the reference's own oracle (or our restatement) on host cores.
 # ---------------------------------------------------------------------------
-def cpu_baseline(shape, sample_tokens: int):
+def cpu_baseline(shape, sample_tokens: int, which: str = "scan"):
+    """The reference's fp64 oracle (helix::ref::scan, or helix::ref::scan_chunked
+    with which="chunked") over the workload's (seq, head) slices on all host
+    cores; `sample_tokens` > 0 times only that many leading tokens."""
     import numpy as np
 
     from helix_b200.synth import make_inputs, to_numpy_f32
@@ -70,7 +83,7 @@ def cpu_baseline(shape, sample_tokens: int):
 
     kind = "reference" if available_reference() else "port"
     impl = Reference() if kind == "reference" else Oracle()
-    T = min(sample_tokens, shape.L)
+    T = min(sample_tokens, shape.L) if sample_tokens > 0 else shape.L
     sub = type(shape)(shape.S, T, shape.H, shape.P, shape.N, shape.G, shape.io)
     t = make_inputs(sub, seed=99)
     prob = {k: np.ascontiguousarray(to_numpy_f32(t[k])) for k in ("s0", "x", "dt", "A", "B", "C")}
@@ -79,7 +92,8 @@ def cpu_baseline(shape, sample_tokens: int):
     y = np.zeros((sub.S, T, sub.H, sub.P), np.float32)
     s1 = np.zeros((sub.S, sub.H, sub.P, sub.N), np.float32)
     F = C.POINTER(C.c_float)
-    fn = getattr(impl.lib, "ref_scan" if kind == "reference" else "oracle_scan")
+    pre = "ref_" if kind == "reference" else "oracle_"
+    fn = getattr(impl.lib, pre + ("scan_chunked" if which == "chunked" else "scan"))
     hpg = sub.H // sub.G
 
     # One call per (seq, head) slice: a descriptor with n_head = n_group = 1
@@ -106,9 +120,11 @@ def cpu_baseline(shape, sample_tokens: int):
         list(ex.map(lambda a: slice_call(*a), jobs))
     sec = time.perf_counter() - t0
     value = sub.S * T / sec  # tokens of the full H-head layer per second
-    return dict(value=value, unit=UNIT, cores=cores, kind=kind,
-                sample=f"{T} of {shape.L} tokens, all {sub.H} heads, S={sub.S}; "
-                       f"{'helix::ref::scan (reference sources)' if kind == 'reference' else 'oracle_scan (C port)'}"
+    name = "helix::ref::scan_chunked" if which == "chunked" else "helix::ref::scan"
+    return dict(value=value, unit=UNIT, cores=cores, kind=kind, seconds=sec,
+                sample=f"{'all ' + str(T) if T == shape.L else str(T) + ' of ' + str(shape.L)} tokens, "
+                       f"all {sub.H} heads, S={sub.S}; "
+                       f"{name + ' (reference sources)' if kind == 'reference' else 'C port of ' + name}"
                        f" per (seq, head) slice on {cores} threads; {sec:.2f} s wall")
 
 
@@ -280,6 +296,60 @@ def bench_lsplit(a, rank: int, world: int, local: int) -> int:
     return 0
 
 
+def pass_figures(shape, info, ms, hbm, tc):
+    """Algorithmic bytes (and flops) of each pass for one scan of `shape` under
+    plan `info`, with the achieved rates of the measured times ms[pass]."""
+    e = 2 if shape.io == "bf16" else 4
+    S, L, H, P, N, G = shape.S, shape.L, shape.H, shape.P, shape.N, shape.G
+    st = S * H * P * N * 4
+    runs = info.state_runs
+    tok_a = min(L, runs * info.run_tokens)
+    # state pass: x, dt and B of the runs it reduces, one state + decay + span per run
+    a_bytes = S * tok_a * (H * P * e + H * 4 + G * N * e) + runs * (st + 3 * S * H * 4)
+    a_flops = 2.0 * S * H * tok_a * P * N
+    # carry pass: run states read, span-entry states written back, s0 and decays read
+    b_bytes = runs * st + max(info.n_spans - 1, 0) * st + st + runs * S * H * 4
+    # output pass: x, B, C, dt read once, y written once, s0 (or span states) read, s1 written
+    c_bytes = S * L * H * P * e + 2 * S * L * G * N * e + S * L * H * 4 + S * L * H * P * 4 + 2 * st
+    out = {}
+    for name, by, fl in (("state", a_bytes, a_flops), ("carry", b_bytes, 0.0), ("output", c_bytes, None)):
+        t = ms.get(name, 0.0)
+        if not t:
+            continue
+        gbs = by / (t * 1e-3) / 1e9
+        d = {"ms": t, "alg_bytes": by, "gbs": gbs, "hbm_frac": gbs / hbm}
+        if fl:
+            d["tflops"] = fl / (t * 1e-3) / 1e12
+            d["tensor_frac"] = d["tflops"] / tc
+        out[name] = d
+    return out, c_bytes
+
+
+def reference_arm(a, shape, rank):
+    if rank != 0:
+        return 0
+    steps = []
+    cb = None
+    for i in range(a.warmup + a.steps):
+        cb = cpu_baseline(shape, a.cpu_sample_tokens)
+        if i >= a.warmup:
+            steps.append(cb["seconds"])
+    sec = statistics.median(steps)
+    v = shape.S * (min(a.cpu_sample_tokens, shape.L) if a.cpu_sample_tokens > 0 else shape.L) / sec
+    cb["value"] = v
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * shape.S * shape.L / v,
+        "higher_is_better": True, "scaling": a.scaling, "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded, BASELINE distributions)",
+        "config": {"workload": f"{a.config}: S={shape.S} L={shape.L} H={shape.H} P={shape.P} "
+                               f"N={shape.N} G={shape.G}; one whole scan per step on the host cores",
+                   "sample": cb["sample"]},
+        "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
+                                    "d2h_bytes_per_step": 0}}), flush=True)
+    return 0
+
+
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -289,36 +359,16 @@ def main():
     from helix_b200.synth import Shape
     if a.lsplit and a.impl != "reference":
         return bench_lsplit(a, rank, world, local)
-    shape = Shape.of(a.config)
-
+    gshape = Shape.of(a.config)
     if a.impl == "reference":
-        if rank != 0:
-            return 0
-        steps = []
-        cb = None
-        for i in range(a.warmup + a.steps):
-            cb = cpu_baseline(shape, a.cpu_sample_tokens)
-            if i >= a.warmup:
-                steps.append(cb["value"])
-        v = statistics.median(steps)
-        cb["value"] = v
-        print(json.dumps({
-            "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": a.gpus,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * shape.S * shape.L / v,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-            "data": "synthetic (seeded, BASELINE distributions)",
-            "config": {"workload": f"{a.config}: S={shape.S} L={shape.L} H={shape.H} P={shape.P} "
-                                   f"N={shape.N} G={shape.G}; CPU sample per step",
-                       "sample": cb["sample"]},
-            "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
-                                        "d2h_bytes_per_step": 0}}), flush=True)
-        return 0
+        return reference_arm(a, gshape, rank)
 
     import torch
     import torch.distributed as dist
 
     import helix_b200
     from helix_b200 import abi
+    from helix_b200 import dist as hdist
     from helix_b200.synth import make_inputs
 
     torch.cuda.set_device(local)
@@ -327,16 +377,30 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
+    strong = a.scaling == "strong" and world > 1
+    if strong:
+        # this rank's whole head groups of the one global problem
+        h0, h1 = hdist.head_slice(gshape.H, gshape.G, rank, world)
+        hpg = gshape.H // gshape.G
+        shape = Shape(gshape.S, gshape.L, h1 - h0, gshape.P, gshape.N, (h1 - h0) // hpg, gshape.io)
+        t = make_inputs(gshape, seed=1000, device=dev, heads=(h0, h1))
+    else:
+        shape = gshape
+        t = make_inputs(shape, seed=1000 + rank, device=dev)
     ctx = helix_b200.Context(local)
-    t = make_inputs(shape, seed=1000 + rank, device=dev)
-    if a.compute == "f32" and shape.io == "bf16":
-        pass  # exact fp32 kernels reading bf16 operands
     x, dt, A, B, Cm, s0 = t["x"], t["dt"], t["A"], t["B"], t["C"], t["s0"]
+    if a.compute == "bf16" and x.dtype != torch.bfloat16 and a.io == "bf16":
+        x, B, Cm = x.to(torch.bfloat16), B.to(torch.bfloat16), Cm.to(torch.bfloat16)
+    if a.io == "f32" and x.dtype != torch.float32:
+        x, B, Cm = x.float(), B.float(), Cm.float()
+    shape = Shape(shape.S, shape.L, shape.H, shape.P, shape.N, shape.G,
+                  "bf16" if x.dtype == torch.bfloat16 else "f32")
     y = torch.empty(x.shape, dtype=torch.float32, device=dev)
     s1 = torch.empty_like(s0)
     d = helix_b200.desc_from_tensors(x, dt, B, s0, y, multipass=True, compute=a.compute)
     if not ctx.supported(d):
         raise SystemExit(f"descriptor unsupported: {ctx.last_error()}")
+    info = ctx.plan_info(d)
     nbytes = ctx.scratch_size(d)
     scratch = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -380,16 +444,14 @@ def main():
         ms = timed(step, a.steps)
     total_ms = max_over_ranks(sum(ms))
     ms_per_step = total_ms / a.steps
-    # tcgen05 family: state + carry kernels when the scratch holds run states,
-    # then the output kernels (fast path, general path); fp32 family: state +
-    # output kernels with runs, the output kernel alone with one
-    has_runs = nbytes >= x.shape[0] * x.shape[2] * x.shape[3] * s0.shape[-1] * 4
-    if a.compute == "bf16":
-        launches = (2 if has_runs else 0) + 2
-    else:
-        launches = 2 if nbytes > 0 else 1
+    # tcgen05 family: state + carry kernels when runs are carried, then the
+    # output kernels (fast path, general path); fp32 family: state kernel
+    # when runs are carried, then the output kernel
+    has_runs = info.state_runs > 0
+    launches = ((2 if has_runs else 0) + 2) if info.family == 1 else ((1 if has_runs else 0) + 1)
+    launches += cast_launches(ctx, d)
 
-    # ---- per-kernel attribution (same steps, passes split) --------------
+    # ---- per-pass attribution (same steps, passes split) --------------
     def only(p):
         def f():
             os.environ["HELIX_ONLY_PASS"] = p
@@ -398,25 +460,24 @@ def main():
             finally:
                 os.environ.pop("HELIX_ONLY_PASS", None)
         return f
-    ms_c = max_over_ranks(sum(timed(only("C"), a.steps))) / a.steps
-    ms_a = max_over_ranks(sum(timed(only("A"), a.steps))) / a.steps if (has_runs or a.compute != "bf16" and nbytes > 0) else 0.0
-    ms_b = max_over_ranks(sum(timed(only("B"), a.steps))) / a.steps if has_runs and a.compute == "bf16" else 0.0
+    ms_pass = {"output": max_over_ranks(sum(timed(only("C"), a.steps))) / a.steps}
+    if has_runs:
+        ms_pass["state"] = max_over_ranks(sum(timed(only("A"), a.steps))) / a.steps
+    if has_runs and info.family == 1:
+        ms_pass["carry"] = max_over_ranks(sum(timed(only("B"), a.steps))) / a.steps
 
     hbm, tc, peak_kind = peaks()
-    e_io = 2 if shape.io == "bf16" else 4
-    n_x = shape.S * shape.L * shape.H * shape.P
-    n_bc = shape.S * shape.L * shape.G * shape.N
-    n_st = shape.S * shape.H * shape.P * shape.N
-    # Output kernel's algorithmic bytes per launch: x, B, C, dt read once,
-    # y written once, s0 read and s1 written once.
-    out_bytes = n_x * e_io + 2 * n_bc * e_io + shape.S * shape.L * shape.H * 4 + n_x * 4 + 2 * n_st * 4
-    achieved = out_bytes / (ms_c * 1e-3) / 1e9
+    passes, out_bytes = pass_figures(shape, info, ms_pass, hbm, tc)
+    achieved = out_bytes / (ms_pass["output"] * 1e-3) / 1e9
     traffic = None  # DRAM bytes per launch of the output kernel, from the committed ncu capture
     tj = ROOT / "profiles" / "ncu_traffic.json"
-    if tj.exists() and a.compute == "bf16":
-        traffic = json.loads(tj.read_text()).get(a.config, {}).get("dram_bytes_per_launch")
+    if tj.exists() and not strong:
+        traffic = json.loads(tj.read_text()).get(f"{a.config}/{a.compute}", {}).get("dram_bytes_per_launch")
+    # tokens of the problem the job processed: the whole head set once
+    # (strong), or one 64-head block per rank (weak)
+    job_tok = gshape.S * gshape.L * (1.0 if strong else world * shape.H / 64.0)
     path_gbs = shape.alg_bytes() / (ms_per_step * 1e-3) / 1e9
-    tflops = shape.flops() / (ms_per_step * 1e-3) / 1e12
+    tflops = (gshape.flops() if strong else world * shape.flops()) / (ms_per_step * 1e-3) / 1e12
 
     # ---- e2e through the C ABI with host buffers ------------------------
     e2e = None
@@ -451,7 +512,7 @@ def main():
 
         def e2e_pipe(K: int) -> float:
             barrier()
-            E = lambda: torch.cuda.Event(enable_timing=True)
+            E = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
             e0 = E()
             e0.record(stream)
             s_in.wait_event(e0)
@@ -490,25 +551,38 @@ def main():
         e2e_pipe(3)
         kp = max(6, a.steps // 4)
         ems = max_over_ranks(e2e_pipe(kp))
-        e2e = {"value": world * shape.S * shape.L / (ems * 1e-3), "unit": UNIT, "ms_per_step": ems,
+        e2e = {"value": job_tok / (ems * 1e-3), "unit": UNIT, "ms_per_step": ems,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "mode": f"{kp} steps in flight on two buffer sets (upload, scan, read-back on separate streams)",
+               "mode": f"{kp} steps in flight on two buffer sets (upload, scan, read-back on separate streams)"
+                       + ("; per rank, its own heads" if world > 1 else ""),
                "serial_ms_per_step": serial_ms}
 
-    value = world * shape.S * shape.L * (shape.H / 64.0) / (ms_per_step * 1e-3)
+    value = job_tok / (ms_per_step * 1e-3)
+    if strong:
+        layout = (f"the problem's {gshape.H} heads split over {world} ranks in whole groups "
+                  f"({shape.H} heads per rank)")
+    elif world > 1:
+        layout = "per rank its own 64-head block of a head-sharded layer"
+    else:
+        layout = "one GPU"
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
-        "warmup": a.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": a.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong" if strong or world == 1 else "weak",
         "vs_baseline": None, "dtype": "bf16" if a.compute == "bf16" else "f32",
         "data": "synthetic (seeded, BASELINE distributions; random A, B, C, x, dt)",
-        "config": {"workload": f"{a.config}: S={shape.S} L={shape.L} H={shape.H} P={shape.P} N={shape.N} "
-                               f"G={shape.G}, x/B/C {shape.io}, dt/A/s0/y/s1 f32, multipass; per rank one "
-                               f"64-head block of a head-sharded layer",
+        "config": {"workload": f"{a.config}: S={gshape.S} L={gshape.L} H={gshape.H} P={gshape.P} "
+                               f"N={gshape.N} G={gshape.G}, x/B/C {shape.io}, dt/A/s0/y/s1 f32, multipass; "
+                               f"{layout}",
                    "l2": "flushed before every timed step (256 MiB write, untimed)",
                    "compute": a.compute, "runs_plan_scratch_bytes": nbytes,
-                   "tflops": tflops, "path_alg_bytes": shape.alg_bytes(), "path_gbs": path_gbs,
-                   "path_hbm_frac": path_gbs / hbm,
-                   "kernels_ms": {"state": ms_a, "carry": ms_b, "output": ms_c}},
+                   "plan": {"family": "tcgen05" if info.family == 1 else "fp32 cuda-core",
+                            "chunk": info.chunk, "run_tokens": info.run_tokens, "n_runs": info.n_runs,
+                            "runs_per_span": info.runs_per_span, "n_spans": info.n_spans,
+                            "state_runs": info.state_runs},
+                   "tflops": tflops, "path_alg_bytes_per_rank": shape.alg_bytes(),
+                   "path_gbs_per_rank": path_gbs, "path_hbm_frac": path_gbs / hbm,
+                   "passes": passes},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic, "kernel": "output kernel",
                      "alg_bytes_per_launch": out_bytes, "peak_kind": peak_kind},
@@ -518,7 +592,8 @@ def main():
     if e2e:
         line["e2e"] = e2e
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(shape, a.cpu_sample_tokens)
+        line["cpu_baseline"] = cpu_baseline(gshape, a.cpu_sample_tokens)
+        line["cpu_baseline_chunked"] = cpu_baseline(gshape, a.cpu_sample_tokens, "chunked")
     if rank == 0:
         print(json.dumps(line), flush=True)
     ctx.close()
@@ -526,6 +601,14 @@ def main():
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     return 0
+
+
+def cast_launches(ctx, d) -> int:
+    """Kernels the scan adds to cast F32-stored x, B, C to bf16 (none when
+    they are stored bf16 or the fp32 family runs)."""
+    info = ctx.plan_info(d)
+    from helix_b200 import abi
+    return 1 if info.family == 1 and d.io_dtype == abi.HELIX_F32 else 0
 
 
 if __name__ == "__main__":

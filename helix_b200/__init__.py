@@ -75,6 +75,13 @@ class Context:
             stream = torch.cuda.current_stream(dev)
         return C.c_void_p(getattr(stream, "cuda_stream", stream))
 
+    def plan_info(self, d: abi.ScanDesc) -> abi.PlanInfo:
+        out = abi.PlanInfo()
+        st = int(self.lib.helix_scan_plan_info(self.handle, C.byref(d), C.byref(out)))
+        if st != abi.HELIX_OK:
+            raise HelixError(st, self.last_error())
+        return out
+
     def shard_state_scratch_size(self, d: abi.ScanDesc) -> int:
         return int(self.lib.helix_scan_shard_state_scratch_size(self.handle, C.byref(d)))
 

@@ -9,6 +9,7 @@
 #include <cstdlib>
 #include <string>
 
+#include "helix/helix_ext.h"
 #include "internal.h"
 
 namespace hx {
@@ -249,4 +250,24 @@ extern "C" const char* helix_ctx_backend_desc(helix_ctx* ctx, const helix_scan_d
     return hx::select_path(*d) == hx::kPathTcBf16
                ? "tcgen05 (bf16 operands, fp32 accumulators and state)"
                : "cuda-core (fp32)";
+}
+
+extern "C" helix_status helix_scan_plan_info(helix_ctx* ctx, const helix_scan_desc* d, helix_plan_info* out) {
+    if (!ctx || !d || !out) return HELIX_ERR_INVALID_ARG;
+    std::string why;
+    if (!hx::supported_impl(ctx, *d, &why)) {
+        hx::set_error(ctx, why);
+        return HELIX_ERR_UNSUPPORTED_SHAPE;
+    }
+    const hx::Plan pl = hx::make_plan(ctx, *d);
+    out->family = pl.path == hx::kPathTcBf16 ? 1 : 0;
+    out->chunk = pl.cs;
+    out->run_tokens = pl.run_tok;
+    out->n_runs = pl.n_runs;
+    out->runs_per_span = pl.out_k;
+    out->n_spans = pl.n_out;
+    out->state_runs = pl.state_runs;
+    out->reserved = 0;
+    out->scratch_bytes = d->multipass ? (uint64_t)pl.total : 0;
+    return HELIX_OK;
 }

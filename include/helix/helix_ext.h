@@ -51,6 +51,28 @@ helix_status helix_scan_encode_static(helix_ctx*             ctx,
                                       helix_tensor           y,
                                       helix_tensor           s1);
 
+/* No counterpart in the reference.  How a descriptor will run: the kernel
+ * family, the chunk the output kernel walks in, and the run cut of the
+ * multipass decomposition (runs of whole 128-token blocks; the output kernel
+ * gives each CTA a span of runs_per_span consecutive runs; the state pass
+ * reduces the state_runs runs before the last span).  For profiling and
+ * capacity planning; host only, nothing is enqueued.  Returns
+ * HELIX_ERR_UNSUPPORTED_SHAPE (and fills nothing) for a descriptor
+ * helix_scan_supported rejects. */
+typedef struct helix_plan_info {
+    int32_t  family;         /* 0: fp32 CUDA-core kernels, 1: tcgen05 bf16 kernels */
+    int32_t  chunk;          /* tokens per chunk of the output kernel */
+    int32_t  run_tokens;     /* tokens per run */
+    int32_t  n_runs;         /* runs per sequence */
+    int32_t  runs_per_span;  /* runs per output CTA */
+    int32_t  n_spans;        /* output spans per sequence */
+    int32_t  state_runs;     /* runs the state pass reduces, per (sequence, head) */
+    int32_t  reserved;
+    uint64_t scratch_bytes;  /* helix_scan_scratch_size() of the descriptor */
+} helix_plan_info;
+
+helix_status helix_scan_plan_info(helix_ctx* ctx, const helix_scan_desc* d, helix_plan_info* out);
+
 /* No counterpart in the reference (one Metal device, one encoder).  Support
  * for cutting every sequence's tokens into contiguous shards, one per GPU
  * ("L-split"): rank k holds tokens [l_k, l_{k+1}) of x, dt, B and C, with d
