@@ -1,0 +1,121 @@
+// scan_cast.cu -- bf16 copies of F32-stored x, B and C for the tensor-core
+// family (reference src/kernels/helix_cast.metal:19-46 and its use in
+// src/runtime/dispatch.mm:232-245, which densify B and C to bf16 for the
+// bf16 Pass C; here x is copied too, because the tensor-core kernels load
+// all three with TMA from bf16 tiles).
+//
+// The copies are dense, in the caller's scratch (Plan::cast regions):
+//   x  -> [S][L][H][Pp]  with Pp = head_dim rounded up to 8 (TMA strides must
+//                        be multiples of 16 bytes); channels P..Pp-1 hold 0
+//   B, C -> [S][L][G][N] (d_state is a multiple of 8)
+// Rounding is to nearest even, the same as the checkers' bf16 widening.
+// HBM-bound: 4 bytes read and 2 written per element, one quad of four
+// consecutive elements per thread step, 16-byte loads where the source rows
+// are contiguous and aligned.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+
+#include "../runtime/internal.h"
+#include "common.cuh"
+
+namespace hx {
+namespace {
+
+constexpr int kCastThreads = 256;
+
+struct CastDst {
+    __nv_bfloat16 *x, *b, *c;
+    int pp;  // padded head_dim of the x copy
+};
+
+__device__ __forceinline__ void put4(__nv_bfloat16* d, float a, float b, float c, float e) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, e);
+    uint2 v;
+    v.x = *reinterpret_cast<uint32_t*>(&lo);
+    v.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(d) = v;
+}
+
+// Four elements cols k..k+3 of one row (elements past `width` are zero).
+__device__ __forceinline__ void cast_quad(const float* row, int64_t stride, int k, int width, __nv_bfloat16* dst) {
+    float v[4];
+    if (stride == 1 && k + 4 <= width && (reinterpret_cast<uintptr_t>(row + k) & 15) == 0) {
+        const float4 f = __ldg(reinterpret_cast<const float4*>(row + k));
+        v[0] = f.x;
+        v[1] = f.y;
+        v[2] = f.z;
+        v[3] = f.w;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = k + e < width ? __ldg(row + (int64_t)(k + e) * stride) : 0.0f;
+    }
+    put4(dst, v[0], v[1], v[2], v[3]);
+}
+
+__global__ void __launch_bounds__(kCastThreads) cast_bf16_kernel(ScanParams p, CastDst d) {
+    const int64_t qx = (int64_t)p.S * p.L * p.H * (d.pp / 4);  // quads of x
+    const int64_t qb = (int64_t)p.S * p.L * p.G * (p.N / 4);   // quads of B (and of C)
+    const int64_t total = qx + 2 * qb;
+    const float* x = static_cast<const float*>(p.x);
+    const float* B = static_cast<const float*>(p.B);
+    const float* C = static_cast<const float*>(p.C);
+    for (int64_t q = (int64_t)blockIdx.x * kCastThreads + threadIdx.x; q < total;
+         q += (int64_t)gridDim.x * kCastThreads) {
+        if (q < qx) {
+            const int64_t r = q / (d.pp / 4);  // (seq, tok, head) row
+            const int k = 4 * (int)(q - r * (d.pp / 4));
+            const int h = (int)(r % p.H);
+            const int64_t st = r / p.H;
+            const int t = (int)(st % p.L), seq = (int)(st / p.L);
+            const float* row = x + (int64_t)seq * p.seq_x + (int64_t)t * p.s_x0 + (int64_t)h * p.s_x1;
+            cast_quad(row, p.s_x2, k, p.P, d.x + r * d.pp + k);
+        } else {
+            const bool isc = q >= qx + qb;
+            const int64_t u = q - qx - (isc ? qb : 0);
+            const int64_t r = u / (p.N / 4);  // (seq, tok, group) row
+            const int k = 4 * (int)(u - r * (p.N / 4));
+            const int g = (int)(r % p.G);
+            const int64_t st = r / p.G;
+            const int t = (int)(st % p.L), seq = (int)(st / p.L);
+            const float* row = isc ? C + (int64_t)seq * p.seq_c + (int64_t)t * p.s_c0 + (int64_t)g * p.s_c1
+                                   : B + (int64_t)seq * p.seq_b + (int64_t)t * p.s_b0 + (int64_t)g * p.s_b1;
+            cast_quad(row, 1, k, p.N, (isc ? d.c : d.b) + r * p.N + k);
+        }
+    }
+}
+
+}  // namespace
+
+int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* stream, bool run) {
+    CastDst d;
+    d.x = static_cast<__nv_bfloat16*>(p->cast_x);
+    d.b = static_cast<__nv_bfloat16*>(p->cast_b);
+    d.c = static_cast<__nv_bfloat16*>(p->cast_c);
+    d.pp = pl.x_pitch;
+    if (run) {
+        const int64_t quads = (int64_t)p->S * p->L * (p->H * (d.pp / 4) + 2 * p->G * (p->N / 4));
+        const int64_t want = (quads + kCastThreads - 1) / kCastThreads;
+        const int64_t cap = (int64_t)(ctx ? ctx->n_sm : 148) * 8;  // grid-stride beyond 8 CTAs per SM
+        const unsigned grid = (unsigned)(want < cap ? (want > 0 ? want : 1) : cap);
+        cast_bf16_kernel<<<grid, kCastThreads, 0, static_cast<cudaStream_t>(stream)>>>(*p, d);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    // the kernels that follow read the dense bf16 copies
+    p->x = d.x;
+    p->s_x0 = (int64_t)p->H * d.pp;
+    p->s_x1 = d.pp;
+    p->s_x2 = 1;
+    p->seq_x = (int64_t)p->L * p->H * d.pp;
+    p->B = d.b;
+    p->C = d.c;
+    p->s_b0 = p->s_c0 = (int64_t)p->G * p->N;
+    p->s_b1 = p->s_c1 = p->N;
+    p->seq_b = p->seq_c = (int64_t)p->L * p->G * p->N;
+    p->io_bf16 = 1;
+    return cudaSuccess;
+}
+
+}  // namespace hx

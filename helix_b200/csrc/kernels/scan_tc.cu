@@ -259,12 +259,15 @@ __device__ __forceinline__ OutTile slab_tile(const PairTile& pt, int v) {
 
 // C and B of one chunk (128 tokens x 128 states each, two 64-state SW128
 // tiles per operand) into st: C at +0, B at +32 KB.
-__device__ __forceinline__ void load_cb_chunk(const TcMaps& maps, uint8_t* st, uint64_t* bar, int g, int t0, int seq) {
+// States nb .. nb + 127: columns past d_state read as zero (TMA fill), so
+// they add nothing to any product.
+__device__ __forceinline__ void load_cb_chunk(const TcMaps& maps, uint8_t* st, uint64_t* bar, int g, int t0, int seq,
+                                              int nb) {
     mbar_expect_tx(bar, 4 * 16384);
-    tma_load_4d(st, &maps.c, bar, 0, g, t0, seq);
-    tma_load_4d(st + 16384, &maps.c, bar, 64, g, t0, seq);
-    tma_load_4d(st + 32768, &maps.b, bar, 0, g, t0, seq);
-    tma_load_4d(st + 49152, &maps.b, bar, 64, g, t0, seq);
+    tma_load_4d(st, &maps.c, bar, nb, g, t0, seq);
+    tma_load_4d(st + 16384, &maps.c, bar, nb + 64, g, t0, seq);
+    tma_load_4d(st + 32768, &maps.b, bar, nb, g, t0, seq);
+    tma_load_4d(st + 49152, &maps.b, bar, nb + 64, g, t0, seq);
 }
 
 // set: 0 for the first slab a CTA runs here, 1 for the second; each has its
@@ -318,7 +321,7 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
     if (warp == kGWarpMma) {
         // ================= TMA producer + MMA issuer ========================
         if (lane == 0) {
-            auto load_cb = [&](int i) { load_cb_chunk(maps, sCB(i), &cb_bar[i & 1], g, t_begin + i * kCS, tl.seq); };
+            auto load_cb = [&](int i) { load_cb_chunk(maps, sCB(i), &cb_bar[i & 1], g, t_begin + i * kCS, tl.seq, p.n_base); };
             auto load_x = [&](int i) {
                 mbar_expect_tx(&bars.x[i & 1], 16384);
                 tma_load_4d(sX(i), &maps.x, &bars.x[i & 1], p0, tl.h, t_begin + i * kCS, tl.seq);
@@ -522,24 +525,27 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
         const bool leader = tid == 384;
         const uint32_t tS = tm + lane_off + T_S;
         {
+            // this lane's state n = n_base + row (none past d_state: zeros)
+            const int n = p.n_base + row;
             const float* src;
             int64_t sc;
             if (ot.run0 == 0) {
                 int sq;
                 src = s0_row(p, tl.seq, &sq) ? p.s0 + (int64_t)sq * p.seq_s + (int64_t)tl.h * p.s_s0 +
-                                                   (int64_t)p0 * p.s_s1 + row
+                                                   (int64_t)p0 * p.s_s1 + n
                                              : nullptr;
                 sc = p.s_s1;
             } else {
-                src = p.agg + (unit0 + ot.run0 - 1) * (int64_t)p.P * p.N + (int64_t)p0 * p.N + row;
+                src = p.agg + (unit0 + ot.run0 - 1) * (int64_t)p.P * p.N + (int64_t)p0 * p.N + n;
                 sc = p.N;
             }
+            const int pn = n < p.N ? pw : 0;
 #pragma unroll 1
             for (int q = 0; q < 8; ++q) {
                 float v[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
-                    v[k] = (8 * q + k < pw) ? (src ? src[(int64_t)(8 * q + k) * sc] : __int_as_float(0x7fc00000)) : 0.0f;
+                    v[k] = (8 * q + k < pn) ? (src ? src[(int64_t)(8 * q + k) * sc] : kNaN) : 0.0f;
                 tmem_st8(tS + 8 * q, *reinterpret_cast<const uint32_t(*)[8]>(v));
                 *reinterpret_cast<uint4*>(sS + sw128_off(row, q)) =
                     make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
@@ -584,8 +590,9 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
             fence_async_smem();
             warp_arrive(&bars.s_ready);
         }
-        if (ok && ot.last) {
-            float* s1 = p.s1 + (int64_t)tl.seq * p.seq_s + (int64_t)tl.h * p.s_s0 + (int64_t)p0 * p.s_s1 + row;
+        if (ok && ot.last && p.n_base + row < p.N) {
+            float* s1 = p.s1 + (int64_t)tl.seq * p.seq_s + (int64_t)tl.h * p.s_s0 + (int64_t)p0 * p.s_s1 + p.n_base +
+                        row;
             tc_fence_after();
 #pragma unroll 1
             for (int q = 0; q < 8; ++q) {
@@ -621,14 +628,27 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
                 if (row < tlen) {
                     if (vec) {
 #pragma unroll
-                        for (int c = 0; c < 4; ++c)
-                            reinterpret_cast<float4*>(yr + 16 * q)[c] =
-                                make_float4(fmaf(e, b[4 * c], a[4 * c]), fmaf(e, b[4 * c + 1], a[4 * c + 1]),
-                                            fmaf(e, b[4 * c + 2], a[4 * c + 2]), fmaf(e, b[4 * c + 3], a[4 * c + 3]));
+                        for (int c = 0; c < 4; ++c) {
+                            float4 v = make_float4(fmaf(e, b[4 * c], a[4 * c]), fmaf(e, b[4 * c + 1], a[4 * c + 1]),
+                                                   fmaf(e, b[4 * c + 2], a[4 * c + 2]),
+                                                   fmaf(e, b[4 * c + 3], a[4 * c + 3]));
+                            float4* dst = reinterpret_cast<float4*>(yr + 16 * q) + c;
+                            if (p.y_add) {
+                                const float4 o = *dst;
+                                v.x += o.x;
+                                v.y += o.y;
+                                v.z += o.z;
+                                v.w += o.w;
+                            }
+                            *dst = v;
+                        }
                     } else {
 #pragma unroll
                         for (int k = 0; k < 16; ++k)
-                            if (16 * q + k < pw) yr[(int64_t)(16 * q + k) * p.s_y2] = fmaf(e, b[k], a[k]);
+                            if (16 * q + k < pw) {
+                                float* dst = yr + (int64_t)(16 * q + k) * p.s_y2;
+                                *dst = fmaf(e, b[k], a[k]) + (p.y_add ? *dst : 0.0f);
+                            }
                     }
                 }
             }
@@ -791,11 +811,14 @@ __device__ __forceinline__ void load_state_tile(const ScanParams& p, const PairT
 #pragma unroll
     for (int v = 0; v < 2; ++v) {
         const SlabRef& sr = pt.s[v];
-        src[v] = pt.run0 == 0 ? p.s0 + (int64_t)sq * p.seq_s + (int64_t)sr.h * p.s_s0 + (int64_t)sr.p0 * p.s_s1
-                              : p.agg + (sr.unit0 + pt.run0 - 1) * (int64_t)p.P * p.N + (int64_t)sr.p0 * p.N;
+        src[v] = (pt.run0 == 0 ? p.s0 + (int64_t)sq * p.seq_s + (int64_t)sr.h * p.s_s0 + (int64_t)sr.p0 * p.s_s1
+                               : p.agg + (sr.unit0 + pt.run0 - 1) * (int64_t)p.P * p.N + (int64_t)sr.p0 * p.N) +
+                 p.n_base;
     }
     const int64_t rs = pt.run0 == 0 ? p.s_s1 : p.N;  // row (channel) stride
-    const bool vec = (rs & 3) == 0 && ((reinterpret_cast<uintptr_t>(src[0]) | reinterpret_cast<uintptr_t>(src[1])) & 15) == 0;
+    const int nw = min(128, p.N - p.n_base);  // states of this half that exist
+    const bool vec = nw == 128 && (rs & 3) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(src[0]) | reinterpret_cast<uintptr_t>(src[1])) & 15) == 0;
     if (vec) {  // 16 float4 per thread (a warp on one 512-byte row), one slab at a time
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -822,7 +845,7 @@ __device__ __forceinline__ void load_state_tile(const ScanParams& p, const PairT
             for (int m = 0; m < 32; ++m) {
                 const int idx = et + 256 * (32 * h + m), r = idx >> 7, n = idx & 127, c = r & 63;
                 const int pw = h ? pt.s[1].pw : pt.s[0].pw;
-                f[m] = c >= pw ? 0.0f : clear ? __ldg(src[h] + (int64_t)c * rs + n) : kNaN;
+                f[m] = (c >= pw || n >= nw) ? 0.0f : clear ? __ldg(src[h] + (int64_t)c * rs + n) : kNaN;
             }
 #pragma unroll
             for (int m = 0; m < 32; ++m) {
@@ -836,9 +859,13 @@ __device__ __forceinline__ void load_state_tile(const ScanParams& p, const PairT
 // s1 of both slabs from st (st_word layout), coalesced: float4 rows when s1
 // allows it, single states otherwise.
 __device__ __forceinline__ void store_state_tile(const ScanParams& p, const PairTile& pt, const float* st, int et) {
-    float* const d0 = p.s1 + (int64_t)pt.seq * p.seq_s + (int64_t)pt.s[0].h * p.s_s0 + (int64_t)pt.s[0].p0 * p.s_s1;
-    float* const d1 = p.s1 + (int64_t)pt.seq * p.seq_s + (int64_t)pt.s[1].h * p.s_s0 + (int64_t)pt.s[1].p0 * p.s_s1;
-    const bool vec = (p.s_s1 & 3) == 0 && ((reinterpret_cast<uintptr_t>(d0) | reinterpret_cast<uintptr_t>(d1)) & 15) == 0;
+    float* const d0 = p.s1 + (int64_t)pt.seq * p.seq_s + (int64_t)pt.s[0].h * p.s_s0 + (int64_t)pt.s[0].p0 * p.s_s1 +
+                      p.n_base;
+    float* const d1 = p.s1 + (int64_t)pt.seq * p.seq_s + (int64_t)pt.s[1].h * p.s_s0 + (int64_t)pt.s[1].p0 * p.s_s1 +
+                      p.n_base;
+    const int nw = min(128, p.N - p.n_base);  // states of this half that exist
+    const bool vec = nw == 128 && (p.s_s1 & 3) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(d0) | reinterpret_cast<uintptr_t>(d1)) & 15) == 0;
     if (vec) {
 #pragma unroll
         for (int m = 0; m < 16; ++m) {
@@ -851,7 +878,8 @@ __device__ __forceinline__ void store_state_tile(const ScanParams& p, const Pair
 #pragma unroll 1
         for (int m = 0; m < 64; ++m) {
             const int idx = et + 256 * m, r = idx >> 7, n = idx & 127, c = r & 63;
-            if (c < ((m >> 5) ? pt.s[1].pw : pt.s[0].pw)) ((m >> 5) ? d1 : d0)[(int64_t)c * p.s_s1 + n] = st[st_word(r, n)];
+            if (c < ((m >> 5) ? pt.s[1].pw : pt.s[0].pw) && n < nw)
+                ((m >> 5) ? d1 : d0)[(int64_t)c * p.s_s1 + n] = st[st_word(r, n)];
         }
     }
 }
@@ -928,7 +956,7 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                     // staged there after G2(i-1), has left it
                     if (!(ok = mbar_wait(&bars.ys_free, (uint32_t)((i - 1) & 1), kWaitBudget))) break;
                     load_cb_chunk(maps, sm + OO_CB + 65536u * (uint32_t)((i + 1) & 1), &cb_bar[(i + 1) & 1], pt.g,
-                                  t_begin + (i + 1) * kCS, pt.seq);
+                                  t_begin + (i + 1) * kCS, pt.seq, p.n_base);
                     cb_issued = i + 2;
                 }
                 if (!(ok = mbar_wait(&bars.xw_ready, par, kWaitBudget))) break;
@@ -1212,7 +1240,10 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0 && sr.pw > 32 * (q & 1)) {
-                        tma_store_4d(&maps.y, yb, sr.p0 + 32 * (q & 1), sr.h, tp + 64 * kh, pt.seq);
+                        if (p.y_add)
+                            tma_reduce_add_4d(&maps.y, yb, sr.p0 + 32 * (q & 1), sr.h, tp + 64 * kh, pt.seq);
+                        else
+                            tma_store_4d(&maps.y, yb, sr.p0 + 32 * (q & 1), sr.h, tp + 64 * kh, pt.seq);
                         bulk_commit();
                     }
                 } else if (c_ok) {
@@ -1226,7 +1257,7 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                         const float fk[4] = {fv.x, fv.y, fv.z, fv.w};
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            if (4 * k4 + e < kmax) *yp = fk[e] * a[4 * k4 + e];
+                            if (4 * k4 + e < kmax) *yp = fk[e] * a[4 * k4 + e] + (p.y_add ? *yp : 0.0f);
                             yp += sy;
                         }
                     }
@@ -1359,7 +1390,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         prefetch_tmap(&maps.b);
         prefetch_tmap(&maps.c);
         for (int i = 0; i < 2 && i < pt.n_ch; ++i)
-            load_cb_chunk(maps, sm + OO_CB + (uint32_t)i * 65536u, &cb_bar[i], pt.g, pt.t_begin + i * kCS, pt.seq);
+            load_cb_chunk(maps, sm + OO_CB + (uint32_t)i * 65536u, &cb_bar[i], pt.g, pt.t_begin + i * kCS, pt.seq,
+                          p.n_base);
     }
     float pre[4 * kPV];  // x of chunk 0 (builders)
     float* st = reinterpret_cast<float*>(sm + OP_XW);  // free until the builders start
@@ -1474,7 +1506,7 @@ __global__ void __launch_bounds__(kOutThreads, 1)
             }
             for (int i = 0; i < 2 && i < pt.n_ch; ++i)
                 load_cb_chunk(maps, sm + OO_CB + (uint32_t)i * 65536u, &cb_bar[2 * v + i], pt.g, pt.t_begin + i * kCS,
-                              pt.seq);
+                              pt.seq, p.n_base);
         }
         out_general(maps, p, slab_tile(pt, v), sm, tm, cb_bar + 2 * v, v);
         tc_fence_before();
@@ -1607,7 +1639,11 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
     const int row = 32 * (warp & 3) + (tid & 31);
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
 
-    const Tile tl = decode_tile(blockIdx.x, p.n_pslab, p.H, runs_in_grid);
+    // states nb .. nb + 127 (a d_state above 128 runs as two halves, half
+    // fastest); lane `row` of the accumulator is state nb + row
+    const int half = (int)blockIdx.x % p.n_half;
+    const int nb = 128 * half;
+    const Tile tl = decode_tile((int)blockIdx.x / p.n_half, p.n_pslab, p.H, runs_in_grid);
     const int p0 = tl.slab * kSlab, pw = min(kSlab, p.P - p0);
     const int g = tl.h / p.hpg;
     const float Ah = p.A[(int64_t)tl.h * p.s_a];
@@ -1657,8 +1693,8 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
     auto load_b = [&](int s) {
         uint64_t* bar = &bars.b_full[s % kStB];
         mbar_expect_tx(bar, 2 * 8192);
-        tma_load_4d(sB(s), &maps.b, bar, 0, g, ts_of(s), tl.seq);
-        tma_load_4d(sB(s) + 8192, &maps.b, bar, 64, g, ts_of(s), tl.seq);
+        tma_load_4d(sB(s), &maps.b, bar, nb, g, ts_of(s), tl.seq);
+        tma_load_4d(sB(s) + 8192, &maps.b, bar, nb + 64, g, ts_of(s), tl.seq);
     };
     auto load_x = [&](int s) {
         uint64_t* bar = &bars.x_full[s % kStX];
@@ -1747,9 +1783,9 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
         }
         if (!ok) atomicCAS(&g_tc_fault, 0u, kFaultMmaState);
         if (lane == 0) lam_total = later / kLog2e;
-        if (ok && lane == 0 && p.run_span && tl.slab == 0)
+        if (ok && lane == 0 && p.run_span && tl.slab == 0 && half == 0)
             p.run_span[((int64_t)tl.seq * p.H + tl.h) * p.n_runs + tl.run] = span_mx;
-        if (ok && p.run_span && tl.slab == 0 && tl.run < p.n_runs - p.state_runs) {
+        if (ok && p.run_span && tl.slab == 0 && half == 0 && tl.run < p.n_runs - p.state_runs) {
             // the last output span has no state pass: run state_runs + r of
             // this head is measured here, four chunks' dt in flight at a time
             const int r2 = p.state_runs + tl.run;
@@ -1809,9 +1845,9 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
         if (ok && n_st > 0)
             ok = st_wait(&bars.xw_empty[(n_st - 1) % kStXw], (uint32_t)(((n_st - 1) / kStXw) & 1), kFaultMmaState);
         tc_fence_after();
-        if (ok) {
+        if (ok && nb + row < p.N) {
             const int64_t unit = ((int64_t)tl.seq * p.H + tl.h) * p.run_slots + tl.run;
-            float* out = p.agg + unit * (int64_t)p.P * p.N + (int64_t)p0 * p.N + row;
+            float* out = p.agg + unit * (int64_t)p.P * p.N + (int64_t)p0 * p.N + nb + row;
             // columns 0..63 hold the hi part, 64..127 the lo part
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2) {
@@ -1829,7 +1865,7 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
     }
     tc_fence_before();
     __syncthreads();
-    if (ok && tid == 0 && tl.slab == 0)
+    if (ok && tid == 0 && tl.slab == 0 && half == 0)
         p.lam[((int64_t)tl.seq * p.H + tl.h) * p.run_slots + tl.run] = lam_total;
     if (is_mma) {
         tc_fence_after();
@@ -1899,9 +1935,16 @@ int configure_tc(const helix_ctx*) {
     return cudaFuncSetAttribute(tc_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_STATE);
 }
 
-int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream) {
+int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void* stream) {
     auto fn = reinterpret_cast<EncodeFn>(ctx->encode_tiled);
     if (!fn) return cudaErrorNotSupported;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const char* only = std::getenv("HELIX_ONLY_PASS");
+    ScanParams p = p_in;
+    if (pl.cast) {  // F32-stored x, B, C: the kernels below read bf16 copies
+        const int e = launch_cast(ctx, pl, &p, stream, !only || *only == 'X');
+        if (e != cudaSuccess) return e;
+    }
     TcMaps maps;
     const int64_t S = p.S;
     // A sequence extent of 1 makes every sequence's token range its own
@@ -1913,11 +1956,9 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* s
         return cudaErrorInvalidValue;
     maps.y_ok = make_y_map(fn, &maps.y, p) ? 1 : 0;
     if (!maps.y_ok) std::memset(&maps.y, 0, sizeof(maps.y));
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const char* only = std::getenv("HELIX_ONLY_PASS");
     const bool do_a = !only || *only == 'A';
     const bool do_c = !only || *only == 'C';
-    const int64_t per_run = (int64_t)p.n_pslab * p.H * S;
+    const int64_t per_run = (int64_t)p.n_pslab * p.H * S * p.n_half;
     if (pl.need_state_kernel && do_a) {
         const int runs = pl.state_runs;
         TcMaps smaps;
@@ -1954,21 +1995,35 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* s
     if (do_c) {
         const int64_t ctas = (int64_t)S * p.G * p.n_pair * p.n_out;
         const int fg = force_general();
-        cudaError_t e = launch(tc_out_kernel, (unsigned)ctas, kPThreads, SMEM_OUT, carry_ran, maps, p, fg);
-        if (e != cudaSuccess) return e;
-        e = launch(tc_out_general_kernel, (unsigned)ctas, kOutThreads, SMEM_OUT, true, maps, p, fg);
-        if (e != cudaSuccess) return e;
+        // one pass per 128 states; the second adds its share of y to the
+        // first's, after it (each output kernel's y writes follow its grid
+        // wait, which the previous pass's general kernel ends last)
+        for (int half = 0; half < p.n_half; ++half) {
+            ScanParams ph = p;
+            ph.n_base = 128 * half;
+            ph.y_add = half > 0;
+            cudaError_t e = launch(tc_out_kernel, (unsigned)ctas, kPThreads, SMEM_OUT, carry_ran || half > 0, maps,
+                                   ph, fg);
+            if (e != cudaSuccess) return e;
+            e = launch(tc_out_general_kernel, (unsigned)ctas, kOutThreads, SMEM_OUT, true, maps, ph, fg);
+            if (e != cudaSuccess) return e;
+        }
     }
     return cudaSuccess;
 }
 
-int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream) {
+int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void* stream) {
     auto fn = reinterpret_cast<EncodeFn>(ctx->encode_tiled);
     if (!fn) return cudaErrorNotSupported;
+    ScanParams p = p_in;
+    if (pl.cast) {
+        const int e = launch_cast(ctx, pl, &p, stream, true);
+        if (e != cudaSuccess) return e;
+    }
     TcMaps maps;
     const int64_t S = p.S;
     if (!make_state_maps(fn, &maps, p)) return cudaErrorInvalidValue;
-    const int64_t per_run = (int64_t)p.n_pslab * p.H * S;
+    const int64_t per_run = (int64_t)p.n_pslab * p.H * S * p.n_half;
     tc_state_kernel<<<(unsigned)(per_run * pl.state_runs), kStThreads, SMEM_STATE, static_cast<cudaStream_t>(stream)>>>(
         maps, p, pl.state_runs);
     return cudaGetLastError();

@@ -51,10 +51,15 @@ size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 //   backend REF or SGMMA          -> exact fp32 (the reference's fp32 paths)
 //   backend MPP                   -> tcgen05 bf16 (the reference's bf16 path)
 //   backend AUTO                  -> compute_dtype decides
+//   F32-stored x, B, C on the tcgen05 family need scratch for their bf16
+//   copies, so single pass takes the fp32 family (as the reference's bf16
+//   Pass C needs its multipass staging, src/runtime/caps.mm:59-72)
 Path select_path(const helix_scan_desc& d) {
     if (d.backend == HELIX_BACKEND_REF || d.backend == HELIX_BACKEND_SGMMA) return kPathSimtF32;
-    if (d.backend == HELIX_BACKEND_MPP) return kPathTcBf16;
-    return d.compute_dtype == HELIX_BF16 ? kPathTcBf16 : kPathSimtF32;
+    const bool tc = d.backend == HELIX_BACKEND_MPP || d.compute_dtype == HELIX_BF16;
+    if (!tc) return kPathSimtF32;
+    if (d.io_dtype == HELIX_F32 && !d.multipass) return kPathSimtF32;
+    return kPathTcBf16;
 }
 
 bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why) {
@@ -88,8 +93,11 @@ bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why) 
 
     // tcgen05 path.
     if (!ctx->tc_ready) return no("tensor-core kernels unavailable on this device");
-    if (d.d_state != 128) return no("bf16 tensor-core path needs d_state == 128");
-    if (d.io_dtype != HELIX_BF16) return no("bf16 tensor-core path needs io_dtype BF16");
+    // 128 states per pass of the kernels (two passes above 128); rows of B
+    // and C are TMA-loaded, so d_state * 2 bytes must be a multiple of 16.
+    if (d.d_state % 8 != 0 || d.d_state > 256)
+        return no("bf16 tensor-core path needs d_state % 8 == 0 and <= 256");
+    if (d.io_dtype == HELIX_F32) return true;  // read through dense bf16 copies
     if (d.s_x[2] != 1) return no("x innermost stride must be 1 for TMA");
     // TMA: every non-innermost global stride must be a multiple of 16 bytes.
     const int64_t tma[] = {d.s_x[0], d.s_x[1], d.seq_x, d.s_b[0], d.s_b[1], d.seq_b,
@@ -148,6 +156,17 @@ void tc_split(const helix_scan_desc& d, int blocks, int n_sm, int max_runs, int*
     *out_k = k;
 }
 
+// The bf16 copies of F32-stored x, B, C at the end of the scratch.
+void add_cast_regions(const helix_scan_desc& d, Plan* pl) {
+    if (!pl->cast) return;
+    pl->x_pitch = (d.head_dim + 7) / 8 * 8;
+    const size_t rows = (size_t)d.n_seq * d.n_tok;
+    pl->off_xc = pl->total;
+    pl->off_bc = pl->off_xc + align256(rows * d.n_head * pl->x_pitch * 2);
+    pl->off_cc = pl->off_bc + align256(rows * d.n_group * d.d_state * 2);
+    pl->total = pl->off_cc + align256(rows * d.n_group * d.d_state * 2);
+}
+
 }  // namespace
 
 Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
@@ -191,7 +210,8 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     // ... and, when a state pass runs, the largest decay span of every run's
     // chunks, measured there, so the output kernel need not read dt for it.
     pl.has_span = pl.has_flags && pl.need_state_kernel;
-    if (pl.run_slots > 0 || pl.has_flags) {
+    pl.cast = d.multipass && pl.path == kPathTcBf16 && d.io_dtype == HELIX_F32;
+    if (pl.run_slots > 0 || pl.has_flags || pl.cast) {
         const size_t agg = (size_t)d.n_seq * d.n_head * pl.run_slots * d.head_dim * d.d_state;
         const size_t lam = (size_t)d.n_seq * d.n_head * pl.run_slots;
         const int64_t units = (int64_t)(d.n_head / d.n_group) * pl.n_pslab;
@@ -202,6 +222,7 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
         const size_t spans = pl.has_span ? (size_t)d.n_seq * d.n_head * pl.n_runs : 0;
         pl.off_span = pl.off_flag + align256(tiles * sizeof(int32_t));
         pl.total = pl.off_span + align256(spans * sizeof(float));
+        add_cast_regions(d, &pl);
     }
     return pl;
 }
@@ -215,11 +236,13 @@ Plan make_shard_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     pl.run_slots = pl.n_runs;
     pl.need_state_kernel = true;
     pl.has_flags = false;
+    pl.has_span = false;
     const size_t agg = (size_t)d.n_seq * d.n_head * pl.run_slots * d.head_dim * d.d_state;
     const size_t lam = (size_t)d.n_seq * d.n_head * pl.run_slots;
     pl.off_agg = 0;
     pl.off_lam = align256(agg * sizeof(float));
     pl.total = pl.off_lam + align256(lam * sizeof(float));
+    add_cast_regions(d, &pl);
     return pl;
 }
 

@@ -137,7 +137,7 @@ helix_status bind_call(helix_ctx* ctx, const helix_scan_desc& d, const Plan& pl,
     p.y = at<float>(t.y);
     p.s1 = at<float>(t.s1);
     p.fault = ctx->fault_word;
-    if (pl.path == kPathTcBf16) {
+    if (pl.path == kPathTcBf16 && !pl.cast) {
         // TMA needs 16-byte aligned global bases.
         const uintptr_t m = reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.B) |
                             reinterpret_cast<uintptr_t>(p.C);
@@ -154,6 +154,11 @@ void bind_scratch(const Plan& pl, char* base, ScanParams* p) {
     p->lam = reinterpret_cast<float*>(base + pl.off_lam);
     p->tile_flag = pl.has_flags ? reinterpret_cast<int32_t*>(base + pl.off_flag) : nullptr;
     p->run_span = pl.has_span ? reinterpret_cast<float*>(base + pl.off_span) : nullptr;
+    if (pl.cast) {
+        p->cast_x = base + pl.off_xc;
+        p->cast_b = base + pl.off_bc;
+        p->cast_c = base + pl.off_cc;
+    }
 }
 
 helix_status run_call(helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream) {
@@ -193,6 +198,9 @@ void fill_params(ScanParams& p, const helix_scan_desc& d, const Plan& pl) {
         p.n_pair = (units + 1) / 2;
     }
     p.io_bf16 = d.io_dtype == HELIX_BF16 ? 1 : 0;
+    p.n_half = (d.d_state + 127) / 128;
+    p.n_base = 0;
+    p.y_add = 0;
     p.dt_min = d.dt_min;
     p.dt_max = d.dt_max;
     p.s_x0 = d.s_x[0]; p.s_x1 = d.s_x[1]; p.s_x2 = d.s_x[2]; p.seq_x = d.seq_x;

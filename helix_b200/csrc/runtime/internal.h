@@ -67,6 +67,13 @@ struct Plan {
     bool   has_flags = false;
     size_t off_span = 0;    // f32 [seq][head][n_runs]: largest decay span of a run's chunks
     bool   has_span = false; // written by the state kernel (tensor-core family with a state pass)
+    // Tensor-core family with x, B, C stored F32: dense bf16 copies made by a
+    // cast kernel first (multipass only; single pass takes the fp32 family).
+    bool   cast     = false;
+    int    x_pitch  = 0;    // channels per row of the x copy (head_dim rounded up to 8)
+    size_t off_xc   = 0;    // bf16 [seq][tok][head][x_pitch]
+    size_t off_bc   = 0;    // bf16 [seq][tok][group][d_state]
+    size_t off_cc   = 0;    // bf16 [seq][tok][group][d_state]
     size_t total    = 0;    // scratch bytes
 };
 
@@ -78,6 +85,11 @@ struct ScanParams {
     int32_t n_pair;         // two-slab tiles per group: ceil(hpg * n_pslab / 2)
     int32_t has_ids;
     int32_t io_bf16;        // x, B, C stored as bf16
+    // Tensor-core family: the kernels cover 128 states at a time.  A d_state
+    // above 128 runs as two halves (n_half = 2): the state kernel covers both
+    // in one grid, the output kernels run once per half with n_base = 0, 128;
+    // the second half adds its share of y to the first's (y_add = 1).
+    int32_t n_half, n_base, y_add;
     float   dt_min, dt_max;
 
     int64_t s_x0, s_x1, s_x2, seq_x;
@@ -101,6 +113,10 @@ struct ScanParams {
     float*         lam;
     int32_t*       tile_flag;  // scratch or null, see Plan
     float*         run_span;   // scratch or null, see Plan
+
+    void*          cast_x;      // scratch: bf16 copies (Plan::cast), else null
+    void*          cast_b;
+    void*          cast_c;
 
     unsigned*      fault;       // the device fault word (helix_device_fault)
     int64_t        s_row_bytes; // bytes one s0 / s1 row spans
@@ -169,6 +185,9 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* s
 // State kernel over every run of the plan (p.agg / p.lam for all n_runs).
 int launch_simt_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+// kernels/scan_cast.cu: when `run`, enqueues the bf16 copies of x, B, C into
+// p->cast_*; then points *p at the copies (dense strides, io_bf16 = 1).
+int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* stream, bool run);
 // kernels/scan_shard.cu
 // state[seq][h] = fold over runs of (exp(lam_r) S + agg_r) from zero, written
 // with the state strides of p (s_s0, s_s1, seq_s); log_decay[seq * H + h] =

@@ -82,9 +82,9 @@ extern "C" helix_status helix_scan_shard_state(helix_ctx* ctx, void* stream, con
     p.A = at<float>(A);
     p.B = at<void>(B);
     p.C = at<void>(C);
-    p.agg = reinterpret_cast<float*>(at<char>(scratch) + pl.off_agg);
-    p.lam = reinterpret_cast<float*>(at<char>(scratch) + pl.off_lam);
-    if (pl.path == hx::kPathTcBf16) {
+    hx::bind_scratch(pl, at<char>(scratch), &p);
+    p.fault = ctx->fault_word;
+    if (pl.path == hx::kPathTcBf16 && !pl.cast) {
         const uintptr_t a = reinterpret_cast<uintptr_t>(p.x) | reinterpret_cast<uintptr_t>(p.B) |
                             reinterpret_cast<uintptr_t>(p.C);
         if (a & 15) {

@@ -10,6 +10,7 @@ bf16 hi+lo pair (~16 mantissa bits), so the carry never passes through a
 single bf16 rounding (the reference's bf16 path keeps its carry fp32 too,
 test_metal_parity.mm:214-218)."""
 import os
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -22,12 +23,14 @@ pytestmark = pytest.mark.gpu
 
 S1_REL, S1_ABS, S1_RL2 = 2e-5, 2e-6, 1e-4
 
-SHAPES = [  # reference tests/test_metal_parity.mm:77-104, d_state = 128 rows
+SHAPES = [  # reference tests/test_metal_parity.mm:77-104 (all 22 rows)
     (1, 1, 2, 64, 128, 1), (7, 1, 2, 64, 128, 1), (63, 1, 2, 64, 128, 1),
     (64, 1, 2, 64, 128, 1), (65, 1, 2, 64, 128, 1), (127, 1, 2, 64, 128, 1),
     (128, 1, 2, 64, 128, 1), (129, 1, 2, 64, 128, 1), (96, 1, 4, 64, 128, 1),
-    (160, 1, 4, 64, 128, 1), (300, 1, 8, 64, 128, 2), (256, 1, 4, 128, 128, 1),
-    (256, 1, 4, 192, 128, 1), (256, 1, 8, 128, 128, 8), (256, 4, 4, 64, 128, 1),
+    (160, 1, 4, 64, 128, 1), (300, 1, 8, 64, 128, 2), (256, 1, 4, 64, 64, 1),
+    (256, 1, 4, 128, 128, 1), (256, 1, 4, 128, 256, 1), (256, 1, 4, 64, 256, 1),
+    (300, 1, 4, 128, 256, 1), (256, 1, 8, 128, 256, 2), (256, 1, 4, 192, 128, 1),
+    (256, 1, 8, 128, 128, 8), (256, 4, 4, 64, 128, 1),
     (1024, 1, 2, 64, 128, 1), (2048, 1, 8, 64, 128, 2), (200, 1, 2, 72, 128, 1),
     # output tiles pair two slabs of a group: an odd slab count leaves the
     # last pair half empty; many pairs make the planner give each output CTA
@@ -172,3 +175,89 @@ def test_no_device_fault_recorded(ctx):
     code = C.c_uint32(123)
     assert ctx.lib.helix_device_fault(ctx.handle, C.byref(code)) == abi.HELIX_OK
     assert code.value == 0
+
+
+# F32-stored x, B, C on the tensor-core family: a cast kernel makes dense bf16
+# copies in the scratch first (the reference's bf16 Pass C casts B and C the
+# same way, src/kernels/helix_cast.metal:19-46).  Shapes cover d_state 64, 128
+# and 256, ragged L, a head_dim that is not a multiple of 64 and several runs.
+F32IO_SHAPES = [(129, 1, 2, 64, 128, 1), (300, 1, 8, 64, 128, 2), (256, 1, 4, 64, 64, 1),
+                (300, 1, 4, 128, 256, 1), (256, 1, 8, 128, 256, 2), (200, 1, 2, 72, 128, 1),
+                (1000, 2, 4, 192, 128, 1), (2048, 1, 8, 64, 128, 2)]
+
+
+@pytest.mark.parametrize("rt", [None, "128"], ids=["planned", "runs128"])
+@pytest.mark.parametrize("shape", F32IO_SHAPES, ids=["L{}S{}H{}P{}N{}G{}".format(*s) for s in F32IO_SHAPES])
+def test_parity_bf16_f32_io(ctx, oracle, run_tokens, shape, rt):
+    prob = oracle.harness_problem(*shape, 4242, True)
+    # the kernels see x, B, C rounded to bf16 once: check their arithmetic on
+    # exactly those values
+    y_ref, s_ref = _oracle(oracle, widen(prob, "bf16"), shape)
+    run_tokens(rt)
+    y, s1, d = run(ctx, prob, multipass=True, io="f32", compute="bf16")
+    assert ctx.select_backend(d) == abi.HELIX_BACKEND_MPP
+    assert "tcgen05" in ctx.backend_desc(d)
+    check_bf16(f"bf16 f32-io {rt} {shape}", y, s1, y_ref, s_ref)
+
+
+def test_f32_io_single_pass_takes_fp32_family(ctx, oracle):
+    """Single pass has no scratch for the bf16 copies: F32-stored inputs with
+    compute BF16 run on the exact fp32 family (as the reference's bf16 Pass C
+    needs multipass)."""
+    shape = (300, 1, 4, 64, 128, 1)
+    prob = oracle.harness_problem(*shape, 4242, True)
+    y_ref, s_ref = _oracle(oracle, prob, shape)
+    y, s1, d = run(ctx, prob, multipass=False, io="f32", compute="bf16")
+    assert ctx.select_backend(d) == abi.HELIX_BACKEND_SGMMA
+    c = compare(y, y_ref, 5e-6, 5e-7)
+    assert c["ok"], c
+
+
+def test_f32_io_strided_x(ctx, oracle):
+    """x read through a view (head rows P + 3 floats apart, channels two
+    floats apart): the cast kernel's strided path."""
+    import torch
+    shape = (300, 2, 4, 64, 128, 2)
+    prob = oracle.harness_problem(*shape, 7, True)
+    y_ref, s_ref = _oracle(oracle, widen(prob, "bf16"), shape)
+
+    L, S, H, P, N, G = shape
+    dev = torch.device("cuda:0")
+    big = torch.full((S, L, H, 2 * P + 3), float("nan"), device=dev)
+    x = big[..., : 2 * P : 2]
+    x.copy_(torch.from_numpy(prob["x"]).to(dev))
+    t = {k: torch.from_numpy(np.ascontiguousarray(prob[k])).to(dev) for k in ("s0", "dt", "A", "B", "C")}
+    import helix_b200
+    y = torch.full((S, L, H, P), float("nan"), device=dev)
+    s1 = torch.full_like(t["s0"], float("nan"))
+    d = helix_b200.desc_from_tensors(x, t["dt"], t["B"], t["s0"], y, multipass=True, compute="bf16")
+    assert ctx.supported(d), ctx.last_error()
+    scratch = torch.empty(ctx.scratch_size(d), dtype=torch.uint8, device=dev)
+    assert ctx.encode(d, t["s0"], x, t["dt"], t["A"], t["B"], t["C"], y, s1, scratch=scratch) == abi.HELIX_OK
+    torch.cuda.synchronize()
+    check_bf16("bf16 f32-io strided x", y.cpu().numpy(), s1.cpu().numpy(), y_ref, s_ref)
+
+
+GOLDEN = sorted((Path(__file__).parent / "golden").glob("*.npz"))
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[p.stem for p in GOLDEN])
+def test_golden_bf16(ctx, oracle, run_tokens, path):
+    """The committed outputs of the reference's own fp64 oracle, on its
+    F32-stored inputs, through the tensor-core family (inputs rounded to bf16
+    by the cast, as the reference's bf16 path rounds its operands).  The
+    rounding of the inputs shows in s1 as well, so both outputs are held to
+    the reference's calibrated bf16 bounds (test_metal_parity.mm:35-38) and
+    the north star's 2e-2 relative L2."""
+    z = np.load(path)
+    L, S, H, P, N, G = (int(v) for v in z["shape"])
+    prob = oracle.harness_problem(L, S, H, P, N, G, int(z["seed"]), bool(z["long_memory"]))
+    ids = z["ids"] if z["ids"].size else None
+    for rt in (None, "128"):
+        run_tokens(rt)
+        y, s1, d = run(ctx, prob, multipass=True, io="f32", compute="bf16", ids=ids)
+        assert "tcgen05" in ctx.backend_desc(d)
+        for name, got, want in (("y", y, z["y"]), ("s1", s1, z["s1"])):
+            c = compare(got, want, BF16_REL, BF16_ABS)
+            record(f"golden bf16 {path.stem} {name} runs={rt}", ratio=c["ratio"], rl2=c["rel_l2"])
+            assert c["ok"] and c["rel_l2"] <= BF16_RL2, (path.stem, name, rt, c)

@@ -39,16 +39,11 @@ ROOT = Path(__file__).resolve().parent.parent
 S1_BF16 = (2e-5, 2e-6, 1e-4)  # the carried state keeps fp32-like bounds on the bf16 path
 
 
-def _problem(seed, L, S, H, P, N, G, hot_chunk=None):
-    """BASELINE distributions; hot_chunk=(t0, h) gives head h one 128-token
-    chunk with softplus(dt) ~ 6 per token (hundreds of nats of decay)."""
-    r = np.random.default_rng(seed)
-    prob = dict(s0=(r.standard_normal((S, H, P, N)) * 0.1).astype(np.float32),
-                x=r.standard_normal((S, L, H, P)).astype(np.float32),
-                dt=(r.standard_normal((S, L, H)) - 4.6).astype(np.float32),
-                A=(-np.exp(r.uniform(0.0, np.log(16.0), H))).astype(np.float32),
-                B=(r.standard_normal((S, L, G, N)) / np.sqrt(N)).astype(np.float32),
-                C=(r.standard_normal((S, L, G, N)) / np.sqrt(N)).astype(np.float32))
+def _problem(oracle, seed, L, S, H, P, N, G, hot_chunk=None):
+    """The reference harness's inputs (the regime the parity bounds are
+    calibrated on); hot_chunk=(t0, h) gives head h one 128-token chunk with
+    softplus(dt) ~ 6 per token (hundreds of nats of decay)."""
+    prob = oracle.harness_problem(L, S, H, P, N, G, seed, True)
     if hot_chunk is not None:
         t0, h = hot_chunk
         prob["dt"][:, t0:t0 + 128, h] = 6.0
@@ -123,7 +118,7 @@ def test_static_two_calls_in_a_row(ctx, oracle, env, compute):
     env("HELIX_RUN_TOKENS", "256")  # 8 runs per sequence: the array carries run states
     shape = (2048, 2, 8, 64, 128, 2)
     for call, seed in enumerate((11, 12)):
-        _check_call(ctx, oracle, _problem(seed, *shape), shape, compute, f"{compute} call {call}")
+        _check_call(ctx, oracle, _problem(oracle, seed, *shape), shape, compute, f"{compute} call {call}")
 
 
 @pytest.mark.parametrize("compute", ["bf16", "f32"])
@@ -131,19 +126,21 @@ def test_static_larger_plan_then_smaller(ctx, oracle, env, compute):
     # first call: 4096 tokens in 16 runs of 256, 8 heads; a hot chunk in head 3
     env("HELIX_RUN_TOKENS", "256")
     big = (4096, 1, 8, 64, 128, 2)
-    _check_call(ctx, oracle, _problem(21, *big, hot_chunk=(1024 + 128, 3)), big, compute, f"{compute} big")
+    _check_call(ctx, oracle, _problem(oracle, 21, *big, hot_chunk=(1024 + 128, 3)), big, compute,
+                f"{compute} big")
     # second call: ragged 1000 tokens, wide heads, one group, the planner's own
     # run cut; a hot chunk in head 1 of the last span
     os.environ.pop("HELIX_RUN_TOKENS", None)
     small = (1000, 2, 4, 128, 128, 1)
-    _check_call(ctx, oracle, _problem(22, *small, hot_chunk=(768, 1)), small, compute, f"{compute} small")
+    _check_call(ctx, oracle, _problem(oracle, 22, *small, hot_chunk=(768, 1)), small, compute,
+                f"{compute} small")
 
 
 def test_static_general_path_forced(ctx, oracle, env):
     env("HELIX_RUN_TOKENS", "256")
     env("HELIX_TC_GENERAL", "1")
     shape = (1536, 1, 4, 64, 128, 2)
-    _check_call(ctx, oracle, _problem(31, *shape), shape, "bf16", "bf16 forced general")
+    _check_call(ctx, oracle, _problem(oracle, 31, *shape), shape, "bf16", "bf16 forced general")
 
 
 def test_static_scratch_rejects_oversized(ctx, cuda, env):
