@@ -228,26 +228,27 @@ def bench_lsplit(a, rank: int, world: int, local: int) -> int:
     gA.manual_seed(9000 + hs)
     t["A"] = -torch.exp(torch.rand(h1 - h0, generator=gA, device=dev) * 2.772588722239781)
     ops = hdist.GpuOps(compute=a.compute)
-    # per step: state kernel + fold, carry combine, then the shard scan (state,
-    # carry and output kernels with several runs, the output kernel alone with one)
     d_scan = helix_b200.desc_from_tensors(t["x"], t["dt"], t["B"], t["s0"], None, multipass=True,
                                           compute=a.compute)
     ctx = helix_b200._ctx_for(t["x"], None)
     n_sb = ctx.scratch_size(d_scan)
     has_runs = n_sb >= t["x"].shape[0] * t["x"].shape[2] * t["x"].shape[3] * t["s0"].shape[-1] * 4
+    # per step: state kernel + fold, carry combine, then the shard scan from
+    # the kept run states (carry kernel with several output spans, output
+    # kernel + general-path kernel; the fp32 family: its output kernel)
     if a.compute == "bf16":
-        launches = 3 + (2 if has_runs else 0) + 2
+        launches = 3 + (1 if has_runs else 0) + 2
     else:
-        launches = 3 + (2 if n_sb else 1)
+        launches = 3 + 1
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     def step():
         if world > 1:
             return hdist.scan_lsplit(t["x"], t["dt"], t["A"], t["B"], t["C"], t["s0"], group=grp, ops=ops)
-        st, ld = ops.shard_state(t["x"], t["dt"], t["A"], t["B"], t["C"])
+        st, ld, keep = ops.shard_state_keep(t["x"], t["dt"], t["A"], t["B"], t["C"])
         carry = ops.carry_combine(t["s0"], st[None][:0], ld[None][:0], None)
-        return ops.scan(t["x"], t["dt"], t["A"], t["B"], t["C"], carry)
+        return ops.scan_shard(t["x"], t["dt"], t["A"], t["B"], t["C"], carry, keep)
 
     def barrier():
         if world > 1:

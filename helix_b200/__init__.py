@@ -14,7 +14,8 @@ from typing import Optional
 
 from . import abi
 
-__all__ = ["HelixError", "Context", "desc_from_tensors", "scan", "shard_state", "carry_combine", "abi"]
+__all__ = ["HelixError", "Context", "desc_from_tensors", "scan", "shard_state", "scan_shard", "carry_combine",
+           "abi"]
 
 
 class HelixError(RuntimeError):
@@ -90,6 +91,11 @@ class Context:
         return int(self.lib.helix_scan_shard_state(
             self.handle, self._stream(stream, x, state), C.byref(d), _t(x), _t(dt), _t(A), _t(B),
             _t(Cm), _t(state), _t(log_decay), _t(scratch)))
+
+    def encode_shard(self, d: abi.ScanDesc, carry, x, dt, A, B, Cm, y, s1, scratch, stream=None) -> int:
+        return int(self.lib.helix_scan_encode_shard(
+            self.handle, self._stream(stream, x, y), C.byref(d), _t(carry), _t(x), _t(dt), _t(A), _t(B),
+            _t(Cm), _t(y), _t(s1), _t(scratch)))
 
     def encode_carry_combine(self, d: abi.ScanDesc, s0, states, log_decays, n_prev: int, carry,
                              ids=None, stream=None) -> int:
@@ -173,12 +179,13 @@ def _ctx_for(x, ctx):
 
 
 def shard_state(x, dt, A, B, Cm, *, compute: str = "auto", backend: int = abi.HELIX_BACKEND_AUTO,
-                ctx: Optional[Context] = None, stream=None):
+                ctx: Optional[Context] = None, stream=None, keep_scratch: bool = False):
     """State this token shard leaves from a zero start, and its log-decay.
 
     x (S, L, H, P), dt (S, L, H), B and Cm (S, L, G, N) hold tokens
     [l0, l1) of every sequence.  Returns (state (S, H, P, N) f32,
-    log_decay (S, H) f32 = sum_t A_h dt_t).  See helix_ext.h."""
+    log_decay (S, H) f32 = sum_t A_h dt_t), plus the scratch holding the
+    run states when keep_scratch (for scan_shard).  See helix_ext.h."""
     import torch
     ctx = _ctx_for(x, ctx)
     S, L, H, P = x.shape
@@ -195,7 +202,27 @@ def shard_state(x, dt, A, B, Cm, *, compute: str = "auto", backend: int = abi.HE
         scratch.record_stream(stream)
     if st != abi.HELIX_OK:
         raise HelixError(st, ctx.last_error())
-    return state, log_decay
+    return (state, log_decay, scratch) if keep_scratch else (state, log_decay)
+
+
+def scan_shard(x, dt, A, B, Cm, carry, scratch, *, compute: str = "auto", backend: int = abi.HELIX_BACKEND_AUTO,
+               ctx: Optional[Context] = None, stream=None):
+    """The shard's scan from `carry`, reusing the run states that
+    shard_state(..., keep_scratch=True) left in `scratch` (no second state
+    pass).  Returns (y, s1)."""
+    import torch
+    ctx = _ctx_for(x, ctx)
+    y = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    s1 = torch.empty(carry.shape, dtype=torch.float32, device=x.device)
+    d = desc_from_tensors(x, dt, B, carry, y, multipass=True, compute=compute, backend=backend)
+    if Cm.stride() != B.stride():
+        d.s_c[:] = list(Cm.stride()[1:]); d.seq_c = Cm.stride(0)
+    st = ctx.encode_shard(d, carry, x, dt, A, B, Cm, y, s1, scratch, stream=stream)
+    if stream is not None and hasattr(stream, "cuda_stream"):
+        scratch.record_stream(stream)
+    if st != abi.HELIX_OK:
+        raise HelixError(st, ctx.last_error())
+    return y, s1
 
 
 def carry_combine(s0, states, log_decays, ids=None, *, ctx: Optional[Context] = None, stream=None):

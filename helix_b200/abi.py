@@ -67,7 +67,7 @@ EXPORTS = (
     # include/helix/helix_ext.h
     "helix_device_fault", "helix_scan_encode_static",
     "helix_scan_shard_state_scratch_size", "helix_scan_shard_state", "helix_scan_carry_combine",
-    "helix_scan_plan_info",
+    "helix_scan_plan_info", "helix_scan_encode_shard",
 )
 
 
@@ -122,6 +122,8 @@ def load(path: Path | str | None = None) -> C.CDLL:
     lib.helix_scan_carry_combine.argtypes = [C.c_void_p, C.c_void_p, P(ScanDesc)] + [Tensor] * 4 + [
         C.c_uint32, Tensor]
     lib.helix_scan_carry_combine.restype = C.c_int
+    lib.helix_scan_encode_shard.argtypes = [C.c_void_p, C.c_void_p, P(ScanDesc)] + [Tensor] * 9
+    lib.helix_scan_encode_shard.restype = C.c_int
     lib.helix_scan_plan_info.argtypes = [C.c_void_p, P(ScanDesc), P(PlanInfo)]
     lib.helix_scan_plan_info.restype = C.c_int
     if path is None:

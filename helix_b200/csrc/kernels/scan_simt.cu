@@ -389,7 +389,7 @@ int launch_simt_t(const Plan& pl, const ScanParams& p, int n_seq, cudaStream_t s
     const bool do_a = !only || *only == 'A';
     const bool do_c = !only || *only == 'C';
     const int64_t per_run = (int64_t)p.n_pslab * p.H;
-    if (pl.need_state_kernel && do_a) {
+    if (pl.need_state_kernel && do_a && !pl.states_ready) {
         const int runs = pl.state_runs;
         simt_state_kernel<CS, NMAX, BF16>
             <<<(unsigned)(per_run * runs * n_seq), kThreads, SM::state_bytes, st>>>(p, runs);

@@ -1942,7 +1942,7 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void
     const char* only = std::getenv("HELIX_ONLY_PASS");
     ScanParams p = p_in;
     if (pl.cast) {  // F32-stored x, B, C: the kernels below read bf16 copies
-        const int e = launch_cast(ctx, pl, &p, stream, !only || *only == 'X');
+        const int e = launch_cast(ctx, pl, &p, stream, !pl.states_ready && (!only || *only == 'X'));
         if (e != cudaSuccess) return e;
     }
     TcMaps maps;
@@ -1956,7 +1956,7 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void
         return cudaErrorInvalidValue;
     maps.y_ok = make_y_map(fn, &maps.y, p) ? 1 : 0;
     if (!maps.y_ok) std::memset(&maps.y, 0, sizeof(maps.y));
-    const bool do_a = !only || *only == 'A';
+    const bool do_a = (!only || *only == 'A') && !pl.states_ready;
     const bool do_c = !only || *only == 'C';
     const int64_t per_run = (int64_t)p.n_pslab * p.H * S * p.n_half;
     if (pl.need_state_kernel && do_a) {

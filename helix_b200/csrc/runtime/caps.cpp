@@ -156,6 +156,27 @@ void tc_split(const helix_scan_desc& d, int blocks, int n_sm, int max_runs, int*
     *out_k = k;
 }
 
+void add_cast_regions(const helix_scan_desc& d, Plan* pl);
+
+// Scratch regions, each 256-byte aligned: run states and run decays
+// (run_slots per head), per-tile path records, per-run decay spans, then the
+// bf16 copies of F32-stored inputs.
+void lay_out_scratch(const helix_scan_desc& d, Plan* pl) {
+    pl->total = 0;
+    if (!(pl->run_slots > 0 || pl->has_flags || pl->cast)) return;
+    const size_t agg = (size_t)d.n_seq * d.n_head * pl->run_slots * d.head_dim * d.d_state;
+    const size_t lam = (size_t)d.n_seq * d.n_head * pl->run_slots;
+    const int64_t units = (int64_t)(d.n_head / d.n_group) * pl->n_pslab;
+    const size_t tiles = pl->has_flags ? (size_t)d.n_seq * d.n_group * ((units + 1) / 2) * pl->n_out : 0;
+    pl->off_agg = 0;
+    pl->off_lam = align256(agg * sizeof(float));
+    pl->off_flag = pl->off_lam + align256(lam * sizeof(float));
+    const size_t spans = pl->has_span ? (size_t)d.n_seq * d.n_head * pl->n_runs : 0;
+    pl->off_span = pl->off_flag + align256(tiles * sizeof(int32_t));
+    pl->total = pl->off_span + align256(spans * sizeof(float));
+    add_cast_regions(d, pl);
+}
+
 // The bf16 copies of F32-stored x, B, C at the end of the scratch.
 void add_cast_regions(const helix_scan_desc& d, Plan* pl) {
     if (!pl->cast) return;
@@ -211,19 +232,7 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     // chunks, measured there, so the output kernel need not read dt for it.
     pl.has_span = pl.has_flags && pl.need_state_kernel;
     pl.cast = d.multipass && pl.path == kPathTcBf16 && d.io_dtype == HELIX_F32;
-    if (pl.run_slots > 0 || pl.has_flags || pl.cast) {
-        const size_t agg = (size_t)d.n_seq * d.n_head * pl.run_slots * d.head_dim * d.d_state;
-        const size_t lam = (size_t)d.n_seq * d.n_head * pl.run_slots;
-        const int64_t units = (int64_t)(d.n_head / d.n_group) * pl.n_pslab;
-        const size_t tiles = pl.has_flags ? (size_t)d.n_seq * d.n_group * ((units + 1) / 2) * pl.n_out : 0;
-        pl.off_agg = 0;
-        pl.off_lam = align256(agg * sizeof(float));
-        pl.off_flag = pl.off_lam + align256(lam * sizeof(float));
-        const size_t spans = pl.has_span ? (size_t)d.n_seq * d.n_head * pl.n_runs : 0;
-        pl.off_span = pl.off_flag + align256(tiles * sizeof(int32_t));
-        pl.total = pl.off_span + align256(spans * sizeof(float));
-        add_cast_regions(d, &pl);
-    }
+    lay_out_scratch(d, &pl);
     return pl;
 }
 
@@ -231,18 +240,14 @@ Plan make_shard_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     helix_scan_desc m = d;
     m.multipass = true;
     Plan pl = make_plan(ctx, m);
-    // every run's state is reduced (the fold needs them all)
+    // every run's state is reduced (the fold needs them all), each run's
+    // decay span measured (tensor-core family): the same scratch then serves
+    // the shard's scan (helix_scan_encode_shard) without a second state pass
     pl.state_runs = pl.n_runs;
     pl.run_slots = pl.n_runs;
     pl.need_state_kernel = true;
-    pl.has_flags = false;
-    pl.has_span = false;
-    const size_t agg = (size_t)d.n_seq * d.n_head * pl.run_slots * d.head_dim * d.d_state;
-    const size_t lam = (size_t)d.n_seq * d.n_head * pl.run_slots;
-    pl.off_agg = 0;
-    pl.off_lam = align256(agg * sizeof(float));
-    pl.total = pl.off_lam + align256(lam * sizeof(float));
-    add_cast_regions(d, &pl);
+    pl.has_span = pl.has_flags;
+    lay_out_scratch(m, &pl);
     return pl;
 }
 

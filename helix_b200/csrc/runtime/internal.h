@@ -75,6 +75,9 @@ struct Plan {
     size_t off_bc   = 0;    // bf16 [seq][tok][group][d_state]
     size_t off_cc   = 0;    // bf16 [seq][tok][group][d_state]
     size_t total    = 0;    // scratch bytes
+    // The run states (and bf16 copies) are already in the scratch, left by
+    // helix_scan_shard_state: no cast and no state kernel run.
+    bool   states_ready = false;
 };
 
 // Kernel parameter block (passed by value).

@@ -131,3 +131,41 @@ extern "C" helix_status helix_scan_carry_combine(helix_ctx* ctx, void* stream, c
     if (rc != cudaSuccess) return launch_error(ctx, rc);
     return HELIX_OK;
 }
+
+extern "C" helix_status helix_scan_encode_shard(helix_ctx* ctx, void* stream, const helix_scan_desc* d,
+                                                helix_tensor carry, helix_tensor x, helix_tensor dt, helix_tensor A,
+                                                helix_tensor B, helix_tensor C, helix_tensor y, helix_tensor s1,
+                                                helix_tensor scratch) {
+    if (!ctx || !d) return HELIX_ERR_INVALID_ARG;
+    if (!carry.buf || !x.buf || !dt.buf || !A.buf || !B.buf || !C.buf || !y.buf || !s1.buf || !scratch.buf) {
+        hx::set_error(ctx, "null tensor");
+        return HELIX_ERR_INVALID_ARG;
+    }
+    helix_scan_desc m = *d;
+    m.multipass = true;
+    std::string why;
+    if (!hx::supported_impl(ctx, m, &why)) {
+        hx::set_error(ctx, why);
+        return HELIX_ERR_UNSUPPORTED_SHAPE;
+    }
+    hx::Plan pl = hx::make_plan(ctx, m);
+    const hx::Plan sp = hx::make_shard_plan(ctx, m);
+    if ((reinterpret_cast<uintptr_t>(at<char>(scratch)) & 255) != 0) {
+        hx::set_error(ctx, "scratch must be 256-byte aligned");
+        return HELIX_ERR_INVALID_ARG;
+    }
+    if (!hx::scratch_fits(at<char>(scratch), sp.total)) {
+        hx::set_error(ctx, "scratch allocation smaller than helix_scan_shard_state_scratch_size()");
+        return HELIX_ERR_SCRATCH_TOO_SMALL;
+    }
+    hx::ScanParams p{};
+    const hx::CallTensors t{carry, x, dt, A, B, C, helix_tensor{nullptr, 0}, y, s1};
+    const helix_status st = hx::bind_call(ctx, m, pl, t, &p);
+    if (st != HELIX_OK) return st;
+    // the shard-state call's layout: a state, decay and decay span for every
+    // run, of which the scan's carry reads the runs before its last span
+    hx::bind_scratch(sp, at<char>(scratch), &p);
+    p.run_slots = sp.run_slots;
+    pl.states_ready = true;
+    return hx::run_call(ctx, pl, p, stream);
+}

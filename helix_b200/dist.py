@@ -16,7 +16,8 @@ Two layouts, combinable as a (head shards x token shards) mesh:
     3. the fold of ranks 0..k-1 onto the sequence's initial state, i.e. the
        exclusive scan of (a1, b1) o (a2, b2) = (a1 a2, a2 b1 + b2)
        (``helix_scan_carry_combine``),
-    4. the ordinary scan of the shard with that carry as s0.
+    4. the scan of the shard with that carry as s0, reusing the run states
+       of step 1 (``helix_scan_encode_shard``; no second state pass).
   The last rank's s1 is every sequence's final state.  The exchange is
   S * H * P * N * 4 bytes per rank (8.4 MB for 8 sequences of 32 heads of
   64 x 128) plus S * H log-decays, over NCCL; it lands in ordinary device
@@ -54,6 +55,18 @@ class GpuOps:
         import helix_b200
         return helix_b200.shard_state(x, dt, A, B, Cm, compute=self.compute, ctx=self.ctx, stream=self.stream)
 
+    def shard_state_keep(self, x, dt, A, B, Cm):
+        """shard_state plus the scratch holding its run states."""
+        import helix_b200
+        return helix_b200.shard_state(x, dt, A, B, Cm, compute=self.compute, ctx=self.ctx, stream=self.stream,
+                                      keep_scratch=True)
+
+    def scan_shard(self, x, dt, A, B, Cm, carry, keep):
+        """The shard's scan from carry, without a second state pass."""
+        import helix_b200
+        return helix_b200.scan_shard(x, dt, A, B, Cm, carry, keep, compute=self.compute, ctx=self.ctx,
+                                     stream=self.stream)
+
     def carry_combine(self, s0, states, log_decays, ids):
         import helix_b200
         return helix_b200.carry_combine(s0, states, log_decays, ids, ctx=self.ctx, stream=self.stream)
@@ -90,10 +103,18 @@ def scan_lsplit(x, dt, A, B, Cm, s0, ids=None, *, group=None, ops: Optional[obje
     ops = ops or GpuOps()
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
-    state, log_decay = ops.shard_state(x, dt, A, B, Cm)
+    # ops that can keep the shard's run states (GpuOps, multipass) scan the
+    # shard from them afterwards, so the state pass runs once per shard
+    keep = None
+    if hasattr(ops, "shard_state_keep") and getattr(ops, "multipass", True):
+        state, log_decay, keep = ops.shard_state_keep(x, dt, A, B, Cm)
+    else:
+        state, log_decay = ops.shard_state(x, dt, A, B, Cm)
     states = [state.new_empty(state.shape) for _ in range(world)]
     decays = [log_decay.new_empty(log_decay.shape) for _ in range(world)]
     dist.all_gather(states, state.contiguous(), group=group)
     dist.all_gather(decays, log_decay.contiguous(), group=group)
     carry = exclusive_carry(ops, s0, states, decays, rank, ids)
+    if keep is not None:
+        return ops.scan_shard(x, dt, A, B, Cm, carry, keep)
     return ops.scan(x, dt, A, B, Cm, carry)

@@ -110,6 +110,25 @@ helix_status helix_scan_shard_state(helix_ctx*             ctx,
                                     helix_tensor           log_decay,
                                     helix_tensor           scratch);
 
+/* No counterpart in the reference.  Step 4 of the L-split above without a
+ * second state pass: the scan of the shard (same d, x, dt, A, B, C as the
+ * helix_scan_shard_state call) starting from `carry`, reading the run states
+ * that call left in `scratch` (the same buffer, untouched since; its
+ * contents are consumed, so call this once per shard-state call).  Writes y
+ * and s1 like helix_scan_encode with s0 = carry and no ids. */
+helix_status helix_scan_encode_shard(helix_ctx*             ctx,
+                                     void*                  stream,
+                                     const helix_scan_desc* d,
+                                     helix_tensor           carry,
+                                     helix_tensor           x,
+                                     helix_tensor           dt,
+                                     helix_tensor           A,
+                                     helix_tensor           B,
+                                     helix_tensor           C,
+                                     helix_tensor           y,
+                                     helix_tensor           s1,
+                                     helix_tensor           scratch);
+
 helix_status helix_scan_carry_combine(helix_ctx*             ctx,
                                       void*                  stream,
                                       const helix_scan_desc* d,

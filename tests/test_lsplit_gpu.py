@@ -109,9 +109,14 @@ def test_carry_combine(ctx, n_prev, with_ids):
     np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("via", ["scan", "scan_shard"])
 @pytest.mark.parametrize("io", ["f32", "bf16"])
 @pytest.mark.parametrize("cuts", [(0, 512, 1024), (0, 100, 613, 640, 1024)], ids=["2shards", "4shards-ragged"])
-def test_lsplit_emulated_on_one_gpu(ctx, oracle, io, cuts):
+def test_lsplit_emulated_on_one_gpu(ctx, oracle, run_tokens, io, cuts, via):
+    """K token shards of one problem on one GPU: shard states, carry
+    combine, shard scans -- through helix_scan_encode with the carry as s0,
+    or through helix_scan_encode_shard on the shard-state scratch (no second
+    state pass)."""
     import helix_b200
     import torch
     shape = (1024, 2, 4, 64, 128, 2)
@@ -123,20 +128,26 @@ def test_lsplit_emulated_on_one_gpu(ctx, oracle, io, cuts):
     t = _torch(prob, io)
     shards = [(a, b) for a, b in zip(cuts[:-1], cuts[1:])]
     sl = lambda k, a, b: t[k][:, a:b].contiguous()
-    pairs = [helix_b200.shard_state(sl("x", a, b), sl("dt", a, b), t["A"], sl("B", a, b), sl("C", a, b), ctx=ctx)
+    run_tokens("128")  # several runs per shard: the run states carry
+    pairs = [helix_b200.shard_state(sl("x", a, b), sl("dt", a, b), t["A"], sl("B", a, b), sl("C", a, b), ctx=ctx,
+                                    keep_scratch=True)
              for a, b in shards]
     states = torch.stack([p[0] for p in pairs]).contiguous()
     lds = torch.stack([p[1] for p in pairs]).contiguous()
     ys, s_last = [], None
     for k, (a, b) in enumerate(shards):
         carry = helix_b200.carry_combine(t["s0"], states[:k].contiguous(), lds[:k].contiguous(), ctx=ctx)
-        y, s_last = helix_b200.scan(sl("x", a, b), sl("dt", a, b), t["A"], sl("B", a, b), sl("C", a, b), carry,
-                                    ctx=ctx)
+        if via == "scan":
+            y, s_last = helix_b200.scan(sl("x", a, b), sl("dt", a, b), t["A"], sl("B", a, b), sl("C", a, b),
+                                        carry, ctx=ctx)
+        else:
+            y, s_last = helix_b200.scan_shard(sl("x", a, b), sl("dt", a, b), t["A"], sl("B", a, b),
+                                              sl("C", a, b), carry, pairs[k][2], ctx=ctx)
         ys.append(y)
     torch.cuda.synchronize()
     y = torch.cat(ys, dim=1).cpu().numpy()
-    _check(f"lsplit y {io} {cuts}", y, y_ref, Y_BOUNDS[io])
-    _check(f"lsplit s1 {io} {cuts}", s_last.cpu().numpy(), s_ref, ST_BOUNDS[io])
+    _check(f"lsplit y {io} {cuts} {via}", y, y_ref, Y_BOUNDS[io])
+    _check(f"lsplit s1 {io} {cuts} {via}", s_last.cpu().numpy(), s_ref, ST_BOUNDS[io])
 
 
 def _nccl_worker(rank, world, port, out_dir):
