@@ -16,6 +16,7 @@ enum : unsigned {
     kFaultTmaState = 3,    // state kernel: a TMA arrival wait ran out
     kFaultMmaState = 4,    // state kernel: an MMA / hand-off wait ran out
     kFaultIdsOverlap = 5,  // an s0 row selected by ids overlaps the s1 rows written
+    kFaultTestStall = 6,   // test hook HELIX_TEST_STALL_CYCLES: a wait nothing ends ran out
 };
 
 constexpr float kNaN = __builtin_nanf("");

@@ -1373,6 +1373,22 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const PairTile pt = pair_tile(p);
     grid_dep_launch();  // the general-path kernel waits for this grid anyway
+    if (p.test_stall > 0) {
+        // Test hook: every thread waits, with the given budget, on an
+        // mbarrier nothing arrives on -- before any copy, MMA or tensor-memory
+        // allocation, so nothing is in flight -- and the expired wait takes
+        // the path every bounded wait of these kernels takes: record the
+        // fault code, return.
+        if (tid == 0) {
+            mbar_init(&cb_bar[0], 1);
+            fence_mbar_init();
+        }
+        __syncthreads();
+        const bool ok = mbar_wait(&cb_bar[0], 0u, p.test_stall);
+        if (!__syncthreads_and(ok) && tid == 0) atomicCAS(&g_tc_fault, 0u, kFaultTestStall);
+        if (tid == 0 && p.tile_flag) p.tile_flag[blockIdx.x] = 1;  // the general kernel leaves it too
+        return;
+    }
     if (tid == 0) {
         mbar_init(&cb_bar[0], 1);
         mbar_init(&cb_bar[1], 1);
@@ -1998,8 +2014,10 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void
         // one pass per 128 states; the second adds its share of y to the
         // first's, after it (each output kernel's y writes follow its grid
         // wait, which the previous pass's general kernel ends last)
+        const char* stall = std::getenv("HELIX_TEST_STALL_CYCLES");
         for (int half = 0; half < p.n_half; ++half) {
             ScanParams ph = p;
+            ph.test_stall = stall ? std::strtoll(stall, nullptr, 10) : 0;
             ph.n_base = 128 * half;
             ph.y_add = half > 0;
             cudaError_t e = launch(tc_out_kernel, (unsigned)ctas, kPThreads, SMEM_OUT, carry_ran || half > 0, maps,

@@ -93,6 +93,9 @@ struct ScanParams {
     // in one grid, the output kernels run once per half with n_base = 0, 128;
     // the second half adds its share of y to the first's (y_add = 1).
     int32_t n_half, n_base, y_add;
+    // Test hook (0 = off): the fast output kernel's CTAs first wait this many
+    // cycles on a barrier nothing arrives on, record kFaultTestStall and return.
+    int64_t test_stall;
     float   dt_min, dt_max;
 
     int64_t s_x0, s_x1, s_x2, seq_x;

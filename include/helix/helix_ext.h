@@ -16,7 +16,11 @@ extern "C" {
  * ctx's device.  Every wait inside those kernels (TMA arrival, tcgen05
  * completion) is bounded; when one expires the kernel releases its tensor
  * memory, returns, and records a nonzero code here instead of hanging the
- * GPU.  *code is 0 when no wait expired.  Synchronous (it copies one word). */
+ * GPU.  *code is 0 when nothing was recorded.  Codes: 1, 2 a wait of the
+ * output kernels (copy arrival; MMA or hand-off), 3, 4 the same in the state
+ * kernel, 5 an s0 row selected by ids overlapped the s1 rows being written
+ * (that sequence's outputs are NaN), 6 the test hook HELIX_TEST_STALL_CYCLES.
+ * Synchronous (it copies one word). */
 helix_status helix_device_fault(helix_ctx* ctx, uint32_t* code);
 
 /* No counterpart in the reference.  The multipass scan for callers that

@@ -204,3 +204,32 @@ def test_bad_device_ordinal():
     with pytest.raises(helix_b200.HelixError) as e:
         helix_b200.Context(10_000)
     assert e.value.status == abi.HELIX_ERR_NO_DEVICE
+
+
+def test_bounded_wait_expires_and_the_gpu_recovers(ctx, oracle):
+    """The tensor-core output kernel's waits are bounded.  With the test hook
+    HELIX_TEST_STALL_CYCLES each of its CTAs first waits, with that short
+    budget, on a barrier nothing arrives on: the wait must run out, the
+    kernel must return (the stream synchronises), the fault word must read
+    code 6 and the tiles it owns stay unwritten.  The next scan on the same
+    context, without the hook, must be correct and record no fault."""
+    import os
+
+    from gpu_harness import BF16_ABS, BF16_REL, run, widen
+    from helpers import compare
+    shape = (512, 1, 4, 64, 128, 2)
+    prob = widen(oracle.harness_problem(*shape, 4242, True), "bf16")
+    d = oracle.desc_init(*shape)
+    y_ref, _ = oracle.scan(d, *[prob[k] for k in ("s0", "x", "dt", "A", "B", "C")])
+    _fault(ctx)  # clear
+    os.environ["HELIX_TEST_STALL_CYCLES"] = "200000"
+    try:
+        y, s1, _ = run(ctx, prob, multipass=True, io="bf16", compute="bf16")
+    finally:
+        os.environ.pop("HELIX_TEST_STALL_CYCLES", None)
+    assert _fault(ctx) == 6
+    assert np.isnan(y).all() and np.isnan(s1).all()
+    y, s1, _ = run(ctx, prob, multipass=True, io="bf16", compute="bf16")
+    assert _fault(ctx) == 0
+    c = compare(y, y_ref, BF16_REL, BF16_ABS)
+    assert c["ok"], c
