@@ -27,9 +27,8 @@
 // scalar A ({1, n_head}; a per-channel A is declined by helix), n_head a
 // multiple of n_group, and at least GGML_HELIX_MIN_TOKENS tokens -- below
 // that the fixed cost of the chunked scan's launches loses to ggml's own
-// per-token kernel (the crossover is measured on B200 by
-// tests/test_length_gate_gpu.py).  ggml applies no clamp to softplus(dt), so
-// neither does the descriptor.
+// per-token kernel (the crossover is measured on B200 by measure_gate.py).
+// ggml applies no clamp to softplus(dt), so neither does the descriptor.
 //
 // Precision.  By default the scan runs on the exact fp32 kernels (ggml's own
 // op test is calibrated at fp32 accuracy, as the reference bridge notes);
@@ -60,9 +59,11 @@
 namespace {
 
 constexpr int kMaxDevices = 64;
-// Below this many tokens the bridge declines (measured crossover on B200,
-// see the header comment); GGML_HELIX_MIN_TOKENS overrides.
-constexpr int kDefaultMinTokens = 64;
+// Below this many tokens the bridge declines.  Measured on B200 against a
+// plain per-token scan kernel (measure_gate.py, 48 heads of 64 x 128): HELIX
+// wins from 16 tokens on the fp32 kernels and from 8 on the tensor cores,
+// and is twice as fast at 32; GGML_HELIX_MIN_TOKENS overrides.
+constexpr int kDefaultMinTokens = 32;
 
 struct Settings {
     bool disabled = false;
