@@ -45,6 +45,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "SSD prefill tok/s and % of TC/HBM roofline, L=8192 H64 P64 N128, 1/2/4/8 B200"
 UNIT = "tok/s"
+BACKENDS = {"auto": 0, "sgmma": 1, "mpp": 2, "ref": 3}  # helix_backend
+FAMILIES = {0: "exact fp32 cuda-core", 1: "tcgen05 bf16", 2: "tcgen05 fp32-class (bf16 hi+lo, three products)"}
 
 
 def parse():
@@ -54,7 +56,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c3")
-    ap.add_argument("--compute", default="bf16", choices=["bf16", "f32"])
+    ap.add_argument("--compute", default="config", choices=["config", "bf16", "f32"],
+                    help="operand precision (default: the config's: bf16 for c3/c5, f32 for c1/c2/c4)")
+    ap.add_argument("--backend", default="auto", choices=["auto", "sgmma", "mpp", "ref"],
+                    help="helix_backend of the descriptor (ref: the exact fp32 CUDA-core kernels)")
     ap.add_argument("--io", default="config", choices=["config", "bf16", "f32"],
                     help="storage of x, B, C (default: the config's)")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
@@ -234,12 +239,13 @@ def bench_lsplit(a, rank: int, world: int, local: int) -> int:
     n_sb = ctx.scratch_size(d_scan)
     has_runs = n_sb >= t["x"].shape[0] * t["x"].shape[2] * t["x"].shape[3] * t["s0"].shape[-1] * 4
     # per step: state kernel + fold, carry combine, then the shard scan from
-    # the kept run states (carry kernel with several output spans, output
-    # kernel + general-path kernel; the fp32 family: its output kernel)
+    # the kept run states (carry kernel with several output spans, then the
+    # output kernel + general-path kernel of the bf16 family, or the one
+    # output kernel of the fp32-class family, which also casts first)
     if a.compute == "bf16":
         launches = 3 + (1 if has_runs else 0) + 2
     else:
-        launches = 3 + 1
+        launches = 4 + (1 if has_runs else 0) + 1
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -312,8 +318,14 @@ def pass_figures(shape, info, ms, hbm, tc):
     b_bytes = runs * st + max(info.n_spans - 1, 0) * st + st + runs * S * H * 4
     # output pass: x, B, C, dt read once, y written once, s0 (or span states) read, s1 written
     c_bytes = S * L * H * P * e + 2 * S * L * G * N * e + S * L * H * 4 + S * L * H * P * 4 + 2 * st
+    # cast pass: x, B, C read as f32, written as bf16 (hi, and lo for the
+    # fp32-class family)
+    planes = 2 if info.family == 2 else 1
+    x_bytes = S * L * (H * P + 2 * G * N)
+    x_bytes = x_bytes * 4 + x_bytes * 2 * planes
     out = {}
-    for name, by, fl in (("state", a_bytes, a_flops), ("carry", b_bytes, 0.0), ("output", c_bytes, None)):
+    for name, by, fl in (("state", a_bytes, a_flops), ("carry", b_bytes, 0.0), ("output", c_bytes, None),
+                         ("cast", x_bytes, None)):
         t = ms.get(name, 0.0)
         if not t:
             continue
@@ -358,6 +370,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
     from helix_b200.synth import Shape
+    if a.compute == "config":
+        a.compute = "bf16" if Shape.of(a.config if not a.lsplit or a.config != "c3" else "c5").io == "bf16" else "f32"
     if a.lsplit and a.impl != "reference":
         return bench_lsplit(a, rank, world, local)
     gshape = Shape.of(a.config)
@@ -398,7 +412,8 @@ def main():
                   "bf16" if x.dtype == torch.bfloat16 else "f32")
     y = torch.empty(x.shape, dtype=torch.float32, device=dev)
     s1 = torch.empty_like(s0)
-    d = helix_b200.desc_from_tensors(x, dt, B, s0, y, multipass=True, compute=a.compute)
+    d = helix_b200.desc_from_tensors(x, dt, B, s0, y, multipass=True, compute=a.compute,
+                                     backend=BACKENDS[a.backend])
     if not ctx.supported(d):
         raise SystemExit(f"descriptor unsupported: {ctx.last_error()}")
     info = ctx.plan_info(d)
@@ -445,12 +460,21 @@ def main():
         ms = timed(step, a.steps)
     total_ms = max_over_ranks(sum(ms))
     ms_per_step = total_ms / a.steps
-    # tcgen05 family: state + carry kernels when runs are carried, then the
-    # output kernels (fast path, general path); fp32 family: state kernel
-    # when runs are carried, then the output kernel
+    # tcgen05 bf16 family: state + carry kernels when runs are carried, then
+    # per 128 states the output kernels (fast path, general path); tcgen05
+    # fp32-class family: state + carry, then one output kernel per 128
+    # states; exact fp32 family: state kernel when runs are carried, then
+    # the output kernel; plus the cast kernel where the plan has one
     has_runs = info.state_runs > 0
-    launches = ((2 if has_runs else 0) + 2) if info.family == 1 else ((1 if has_runs else 0) + 1)
-    launches += cast_launches(ctx, d)
+    n_half = (shape.N + 127) // 128
+    if info.family == 1:
+        launches = (2 if has_runs else 0) + 2 * n_half
+    elif info.family == 2:
+        launches = (2 if has_runs else 0) + n_half
+    else:
+        launches = (1 if has_runs else 0) + 1
+    n_cast = cast_launches(ctx, d)
+    launches += n_cast
 
     # ---- per-pass attribution (same steps, passes split) --------------
     def only(p):
@@ -464,11 +488,23 @@ def main():
     ms_pass = {"output": max_over_ranks(sum(timed(only("C"), a.steps))) / a.steps}
     if has_runs:
         ms_pass["state"] = max_over_ranks(sum(timed(only("A"), a.steps))) / a.steps
-    if has_runs and info.family == 1:
+    if has_runs and info.family in (1, 2):
         ms_pass["carry"] = max_over_ranks(sum(timed(only("B"), a.steps))) / a.steps
+    if n_cast:
+        ms_pass["cast"] = max_over_ranks(sum(timed(only("X"), a.steps))) / a.steps
 
     hbm, tc, peak_kind = peaks()
     passes, out_bytes = pass_figures(shape, info, ms_pass, hbm, tc)
+    if info.family in (1, 2):
+        # MMA work the output kernels issue per scan (bf16 flops, every pass
+        # of every GEMM at its full tile), against measured bf16 peak
+        units = shape.S * shape.H * ((shape.P + 63) // 64) * ((shape.L + 127) // 128) * n_half
+        per_unit = 2 * 128 * 128 * 128 * 3 + 9 * 2 * 128 * 64 * 128 if info.family == 2 else \
+            (2 * 128 * 128 * 128 * 5) / 2  # bf16: five 128-cube GEMMs per pair of slabs
+        mma = units * per_unit
+        passes["output"]["mma_flops"] = mma
+        passes["output"]["mma_tflops"] = mma / (ms_pass["output"] * 1e-3) / 1e12
+        passes["output"]["mma_tensor_frac"] = passes["output"]["mma_tflops"] / tc
     achieved = out_bytes / (ms_pass["output"] * 1e-3) / 1e9
     traffic = None  # DRAM bytes per launch of the output kernel, from the committed ncu capture
     tj = ROOT / "profiles" / "ncu_traffic.json"
@@ -577,7 +613,8 @@ def main():
                                f"{layout}",
                    "l2": "flushed before every timed step (256 MiB write, untimed)",
                    "compute": a.compute, "runs_plan_scratch_bytes": nbytes,
-                   "plan": {"family": "tcgen05" if info.family == 1 else "fp32 cuda-core",
+                   "backend": a.backend,
+                   "plan": {"family": FAMILIES.get(info.family, str(info.family)),
                             "chunk": info.chunk, "run_tokens": info.run_tokens, "n_runs": info.n_runs,
                             "runs_per_span": info.runs_per_span, "n_spans": info.n_spans,
                             "state_runs": info.state_runs},
@@ -605,11 +642,12 @@ def main():
 
 
 def cast_launches(ctx, d) -> int:
-    """Kernels the scan adds to cast F32-stored x, B, C to bf16 (none when
-    they are stored bf16 or the fp32 family runs)."""
+    """Kernels the scan adds to cast F32-stored x, B, C to bf16 (the bf16
+    family with F32 storage, and the fp32-class family, which always reads
+    bf16 hi | lo pairs; none for the exact fp32 family)."""
     info = ctx.plan_info(d)
     from helix_b200 import abi
-    return 1 if info.family == 1 and d.io_dtype == abi.HELIX_F32 else 0
+    return 1 if (info.family == 1 and d.io_dtype == abi.HELIX_F32) or info.family == 2 else 0
 
 
 if __name__ == "__main__":

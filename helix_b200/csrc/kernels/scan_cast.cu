@@ -9,9 +9,12 @@
 //                        be multiples of 16 bytes); channels P..Pp-1 hold 0
 //   B, C -> [S][L][G][N] (d_state is a multiple of 8)
 // Rounding is to nearest even, the same as the checkers' bf16 widening.
-// HBM-bound: 4 bytes read and 2 written per element, one quad of four
-// consecutive elements per thread step, 16-byte loads where the source rows
-// are contiguous and aligned.
+// For the three-product family (scan_tc3.cu) the kernel also writes the low
+// halves, lo = bf16(v - hi), into copies of the same layout: hi + lo carries
+// v to about 16 significant bits.
+// HBM-bound: 4 bytes read and 2 (4 with the low halves) written per element,
+// one quad of four consecutive elements per thread step, 16-byte loads where
+// the source rows are contiguous and aligned.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -27,19 +30,32 @@ constexpr int kCastThreads = 256;
 
 struct CastDst {
     __nv_bfloat16 *x, *b, *c;
+    __nv_bfloat16 *xl, *bl, *cl;  // low halves (three-product family), else null
     int pp;  // padded head_dim of the x copy
 };
 
-__device__ __forceinline__ void put4(__nv_bfloat16* d, float a, float b, float c, float e) {
+__device__ __forceinline__ uint2 bf16x4(float a, float b, float c, float e) {
     __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, e);
     uint2 v;
     v.x = *reinterpret_cast<uint32_t*>(&lo);
     v.y = *reinterpret_cast<uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(d) = v;
+    return v;
+}
+
+// v rounded to bf16 at d; with dl, also the rounding residual v - hi at dl.
+__device__ __forceinline__ void put4(__nv_bfloat16* d, __nv_bfloat16* dl, const float (&v)[4]) {
+    const uint2 h = bf16x4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<uint2*>(d) = h;
+    if (dl) {
+        const float h0 = __uint_as_float(h.x << 16), h1 = __uint_as_float(h.x & 0xffff0000u);
+        const float h2 = __uint_as_float(h.y << 16), h3 = __uint_as_float(h.y & 0xffff0000u);
+        *reinterpret_cast<uint2*>(dl) = bf16x4(v[0] - h0, v[1] - h1, v[2] - h2, v[3] - h3);
+    }
 }
 
 // Four elements cols k..k+3 of one row (elements past `width` are zero).
-__device__ __forceinline__ void cast_quad(const float* row, int64_t stride, int k, int width, __nv_bfloat16* dst) {
+__device__ __forceinline__ void cast_quad(const float* row, int64_t stride, int k, int width, __nv_bfloat16* dst,
+                                          __nv_bfloat16* dst_lo) {
     float v[4];
     if (stride == 1 && k + 4 <= width && (reinterpret_cast<uintptr_t>(row + k) & 15) == 0) {
         const float4 f = __ldg(reinterpret_cast<const float4*>(row + k));
@@ -51,7 +67,7 @@ __device__ __forceinline__ void cast_quad(const float* row, int64_t stride, int 
 #pragma unroll
         for (int e = 0; e < 4; ++e) v[e] = k + e < width ? __ldg(row + (int64_t)(k + e) * stride) : 0.0f;
     }
-    put4(dst, v[0], v[1], v[2], v[3]);
+    put4(dst, dst_lo, v);
 }
 
 __global__ void __launch_bounds__(kCastThreads) cast_bf16_kernel(ScanParams p, CastDst d) {
@@ -70,7 +86,7 @@ __global__ void __launch_bounds__(kCastThreads) cast_bf16_kernel(ScanParams p, C
             const int64_t st = r / p.H;
             const int t = (int)(st % p.L), seq = (int)(st / p.L);
             const float* row = x + (int64_t)seq * p.seq_x + (int64_t)t * p.s_x0 + (int64_t)h * p.s_x1;
-            cast_quad(row, p.s_x2, k, p.P, d.x + r * d.pp + k);
+            cast_quad(row, p.s_x2, k, p.P, d.x + r * d.pp + k, d.xl ? d.xl + r * d.pp + k : nullptr);
         } else {
             const bool isc = q >= qx + qb;
             const int64_t u = q - qx - (isc ? qb : 0);
@@ -81,7 +97,8 @@ __global__ void __launch_bounds__(kCastThreads) cast_bf16_kernel(ScanParams p, C
             const int t = (int)(st % p.L), seq = (int)(st / p.L);
             const float* row = isc ? C + (int64_t)seq * p.seq_c + (int64_t)t * p.s_c0 + (int64_t)g * p.s_c1
                                    : B + (int64_t)seq * p.seq_b + (int64_t)t * p.s_b0 + (int64_t)g * p.s_b1;
-            cast_quad(row, 1, k, p.N, (isc ? d.c : d.b) + r * p.N + k);
+            __nv_bfloat16* lo = isc ? d.cl : d.bl;
+            cast_quad(row, 1, k, p.N, (isc ? d.c : d.b) + r * p.N + k, lo ? lo + r * p.N + k : nullptr);
         }
     }
 }
@@ -93,6 +110,9 @@ int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* strea
     d.x = static_cast<__nv_bfloat16*>(p->cast_x);
     d.b = static_cast<__nv_bfloat16*>(p->cast_b);
     d.c = static_cast<__nv_bfloat16*>(p->cast_c);
+    d.xl = static_cast<__nv_bfloat16*>(p->cast_xl);
+    d.bl = static_cast<__nv_bfloat16*>(p->cast_bl);
+    d.cl = static_cast<__nv_bfloat16*>(p->cast_cl);
     d.pp = pl.x_pitch;
     if (run) {
         const int64_t quads = (int64_t)p->S * p->L * (p->H * (d.pp / 4) + 2 * p->G * (p->N / 4));
@@ -103,7 +123,8 @@ int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* strea
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    // the kernels that follow read the dense bf16 copies
+    // the kernels that follow read the dense bf16 copies (and the low
+    // halves, with the same strides, from p->cast_xl / cast_bl / cast_cl)
     p->x = d.x;
     p->s_x0 = (int64_t)p->H * d.pp;
     p->s_x1 = d.pp;

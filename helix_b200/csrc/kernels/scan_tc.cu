@@ -24,6 +24,7 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "tc_shared.cuh"
 #include "umma.cuh"
 
 namespace hx {
@@ -35,16 +36,10 @@ __device__ unsigned int g_tc_fault = 0;
 namespace {
 
 using namespace umma;
-
-constexpr int kCS = 128;
-constexpr long long kWaitBudget = 1ll << 31;  // clock cycles, ~1 s
+using namespace tc;
 
 
-struct TcMaps {
-    CUtensorMap x, b, c;
-    CUtensorMap y;  // fp32 y in 32-channel x 64-token boxes (fast output path)
-    int y_ok;       // y could be described by a tensor map
-};
+
 
 // TMEM columns.
 constexpr uint32_t ID_G4W = idesc_bf16(128, 128, true, true);
@@ -53,65 +48,7 @@ constexpr uint32_t ID_G1 = idesc_bf16(128, 128, false, false);
 constexpr uint32_t ID_G2 = idesc_bf16(128, 64, false, true);
 constexpr uint32_t ID_G3 = idesc_bf16(128, 64, false, true);
 
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
 
-// Descriptor of a shared-memory address `off` bytes past the one `base`
-// describes.  Shared addresses stay below 256 KB, so the 14-bit start field
-// never carries into the next field and the offset simply adds.
-__device__ __forceinline__ uint64_t desc_add(uint64_t base, uint32_t off) { return base + (uint64_t)(off >> 4); }
-__device__ __forceinline__ uint32_t kmajor_off(int ks) { return (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u; }
-
-// K-major operand: K step ks (16 elements) of a 2-tile (K = 128) operand.
-__device__ __forceinline__ uint64_t desc_kmajor(uint32_t base, int ks) {
-    return sdesc_sw128(base + (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u, 16, 1024);
-}
-// MN-major operand: K step ks = 16 rows of 128 B; M/N tiles 16 KB apart.
-__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t base, int ks) {
-    return sdesc_sw128(base + (uint32_t)ks * 2048u, 16384, 1024);
-}
-
-// ---------------------------------------------------------------------------
-// Chunk vectors computed by one warp (no block barriers): lane l owns the
-// four tokens 4l..4l+3 of the 128-token chunk.  Returns, for those tokens,
-// dt (0 past the chunk end) and the inclusive prefix of A*dt in log2 units;
-// *total gets the chunk's sum of A*dt (log2 units).
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void warp_chunk_prefix(const ScanParams& p, int64_t db, int t0, int tlen, float Ah2,
-                                                  const float (&raw)[4], float (&v)[4], float (&pre)[4],
-                                                  float* total) {
-    const int lane = threadIdx.x & 31;
-    float run = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        v[k] = (4 * lane + k < tlen) ? dt_of(raw[k], p.dt_min, p.dt_max) : 0.0f;
-        run += Ah2 * v[k];
-        pre[k] = run;
-    }
-    float incl = run;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const float u = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += u;
-    }
-    const float excl = incl - run;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) pre[k] += excl;
-    *total = __shfl_sync(0xffffffffu, incl, 31);
-}
-
-// Raw dt of tokens t0 + 4 lane .. +3.  Tokens at or past t_end read token
-// t_end - 1 instead (every consumer masks them by the chunk length): the loads
-// carry no condition, so nothing waits for them before their first use.
-__device__ __forceinline__ void warp_load_dt(const ScanParams& p, int64_t db, int t0, int t_end, float (&raw)[4]) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int t = min(t0 + 4 * lane + k, t_end - 1);
-        raw[k] = __ldg(p.dt + db + (int64_t)t * p.s_dt0);
-    }
-}
 
 // ---------------------------------------------------------------------------
 // Output kernel: warp roles with the accumulators, M' and the carried state
@@ -152,7 +89,6 @@ constexpr int kVec = 5 * 128 + 16;        // floats per ring slot: dt | Lc2 | w 
 constexpr uint32_t SMEM_OUT = OO_V + kRing * kVec * 4 + 1024;
 constexpr int kOutThreads = 640;          // 20 warps: 96 registers per thread
 constexpr uint32_t T_D1 = 0, T_M = 128, T_D2 = 192, T_D3 = 256, T_D4 = 384, T_S = 448;
-constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kSpanMax2 = 20.0f * kLog2e;
 constexpr uint32_t ID_G4 = idesc_bf16(128, 64, true, true);
 
@@ -1611,23 +1547,35 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
 constexpr int kStEpi = 256;
 constexpr int kStThreads = kStEpi + 64;
 constexpr int kStHalf = 64;                            // tokens per step
-// Two-deep B and x rings and one xw buffer keep a CTA at 69 KB of shared
-// memory, so three CTAs share an SM: more CTAs in flight hide the load
-// latency of each step better than deeper rings in fewer CTAs.
-constexpr int kStB = 2;                                // B ring depth
-constexpr int kStX = 2;                                // x ring depth
-constexpr int kStXw = 1;                               // xw buffers
-constexpr int kStCtas = 3;                             // CTAs per SM
 constexpr int kStRing = 4;
-constexpr uint32_t SO_B = 0;                           // kStB x 16 KB: B rows of one step, states 0-63 | 64-127
-constexpr uint32_t SO_X = SO_B + kStB * 16384;         // kStX x 8 KB: x rows of one step
-constexpr uint32_t SO_XW = SO_X + kStX * 8192;         // kStXw x (hi 8 KB | lo 8 KB)
-constexpr uint32_t SO_W = SO_XW + kStXw * 16384;       // kStRing x 128 weights
-constexpr uint32_t SO_DT = SO_W + kStRing * 512;         // vector warp's raw dt ring, 4 x 128 floats
-constexpr uint32_t SMEM_STATE = SO_DT + 4 * 512 + 1024;
+// Shared-memory plan of the state kernel.  bf16: two-deep B and x rings and
+// one xw buffer keep a CTA at 69 KB, so three CTAs share an SM: more CTAs in
+// flight hide the load latency of each step better than deeper rings in
+// fewer CTAs.  Three-product mode (X3): B and x slots hold hi | lo halves,
+// the x ring is one deep, and two CTAs share an SM.
+template <bool X3>
+struct StCfg {
+    static constexpr int B = 2;                        // B ring depth
+    static constexpr int X = X3 ? 1 : 2;               // x ring depth
+    static constexpr int Xw = 1;                       // xw buffers
+    static constexpr int Ctas = X3 ? 2 : 3;            // CTAs per SM
+    static constexpr uint32_t b_slot = X3 ? 32768 : 16384;  // B rows of one step: states 0-63 | 64-127 (| lo)
+    static constexpr uint32_t x_slot = X3 ? 16384 : 8192;   // x rows of one step (| lo)
+    static constexpr uint32_t SO_B = 0;
+    static constexpr uint32_t SO_X = SO_B + B * b_slot;
+    static constexpr uint32_t SO_XW = SO_X + X * x_slot;        // Xw x (hi 8 KB | lo 8 KB)
+    static constexpr uint32_t SO_W = SO_XW + Xw * 16384;        // kStRing x 128 weights
+    static constexpr uint32_t SO_DT = SO_W + kStRing * 512;     // vector warp's raw dt ring, 4 x 128 floats
+    static constexpr uint32_t SMEM = SO_DT + 4 * 512 + 1024;
+};
+static_assert(StCfg<false>::Ctas == kStateCtasPerSm && StCfg<true>::Ctas == kStateCtasPerSmX3,
+              "the run planner's state-kernel occupancy");
+constexpr uint32_t SMEM_STATE = StCfg<false>::SMEM;
+constexpr uint32_t SMEM_STATE_X3 = StCfg<true>::SMEM;
+constexpr uint32_t ID_G4W64 = idesc_bf16(128, 64, true, true);
 
 struct StBars {
-    uint64_t b_full[kStB], b_done[kStB], x_full[kStX], xw_full[kStXw], xw_empty[kStXw];
+    uint64_t b_full[2], b_done[2], x_full[2], xw_full[1], xw_empty[1];
     uint64_t w_full[kStRing], w_empty[kStRing];
 };
 
@@ -1640,8 +1588,16 @@ __device__ __forceinline__ bool st_wait(uint64_t* bar, uint32_t parity, unsigned
     return all;
 }
 
-__global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __grid_constant__ TcMaps maps, ScanParams p,
-                                                                 int runs_in_grid) {
+//
+// X3 (three-product family): B and x come as bf16 hi | lo pairs; xw is
+// w (x_hi + x_lo) split again, and each K step adds B_lo . xw_hi (N = 64)
+// into the hi columns, so the state is B_hi xw_hi + B_hi xw_lo + B_lo xw_hi.
+template <bool X3>
+__global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
+    tc_state_kernel(const __grid_constant__ TcMaps maps, ScanParams p, int runs_in_grid) {
+    using Cfg = StCfg<X3>;
+    constexpr int kStB = Cfg::B, kStX = Cfg::X, kStXw = Cfg::Xw;
+    constexpr uint32_t SO_B = Cfg::SO_B, SO_X = Cfg::SO_X, SO_XW = Cfg::SO_XW, SO_W = Cfg::SO_W, SO_DT = Cfg::SO_DT;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
     float* wring = reinterpret_cast<float*>(sm + SO_W);
@@ -1678,8 +1634,8 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
         warp_load_dt(p, db, t0_of(min(1, n_ch - 1)), t_end, r1);
         warp_load_dt(p, db, t0_of(min(2, n_ch - 1)), t_end, r2);
     }
-    auto sB = [&](int s) { return sm + SO_B + (uint32_t)(s % kStB) * 16384u; };
-    auto sX = [&](int s) { return sm + SO_X + (uint32_t)(s % kStX) * 8192u; };
+    auto sB = [&](int s) { return sm + SO_B + (uint32_t)(s % kStB) * Cfg::b_slot; };
+    auto sX = [&](int s) { return sm + SO_X + (uint32_t)(s % kStX) * Cfg::x_slot; };
     auto sXW = [&](int s) { return sm + SO_XW + (uint32_t)(s % kStXw) * 16384u; };
 
     if (tid == 0) {
@@ -1708,14 +1664,19 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
 
     auto load_b = [&](int s) {
         uint64_t* bar = &bars.b_full[s % kStB];
-        mbar_expect_tx(bar, 2 * 8192);
+        mbar_expect_tx(bar, (X3 ? 4 : 2) * 8192);
         tma_load_4d(sB(s), &maps.b, bar, nb, g, ts_of(s), tl.seq);
         tma_load_4d(sB(s) + 8192, &maps.b, bar, nb + 64, g, ts_of(s), tl.seq);
+        if constexpr (X3) {
+            tma_load_4d(sB(s) + 16384, &maps.bl, bar, nb, g, ts_of(s), tl.seq);
+            tma_load_4d(sB(s) + 24576, &maps.bl, bar, nb + 64, g, ts_of(s), tl.seq);
+        }
     };
     auto load_x = [&](int s) {
         uint64_t* bar = &bars.x_full[s % kStX];
-        mbar_expect_tx(bar, 8192);
+        mbar_expect_tx(bar, (X3 ? 2 : 1) * 8192);
         tma_load_4d(sX(s), &maps.x, bar, p0, tl.h, ts_of(s), tl.seq);
+        if constexpr (X3) tma_load_4d(sX(s) + 8192, &maps.xl, bar, p0, tl.h, ts_of(s), tl.seq);
     };
 
     bool ok = true;
@@ -1723,6 +1684,10 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
         if ((tid & 31) == 0) {
             prefetch_tmap(&maps.b);
             prefetch_tmap(&maps.x);
+            if constexpr (X3) {
+                prefetch_tmap(&maps.bl);
+                prefetch_tmap(&maps.xl);
+            }
             for (int s = 0; s < kStB && s < n_st; ++s) load_b(s);
             for (int s = 0; s < kStX && s < n_st; ++s) load_x(s);
             for (int s = 0; s < n_st && ok; ++s) {
@@ -1737,6 +1702,13 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks)
                     mma_bf16(tm, desc_add(dA, 2048u * ks), desc_add(dX, 2048u * ks), ID_G4W, (s > 0 || ks > 0) ? 1u : 0u);
+                if constexpr (X3) {
+                    // B_lo . xw_hi into the hi columns
+                    const uint64_t dAl = sdesc_sw128(smem_u32(sB(s)) + 16384u, 8192, 1024);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        mma_bf16(tm, desc_add(dAl, 2048u * ks), desc_add(dX, 2048u * ks), ID_G4W64, 1u);
+                }
                 mma_commit(&bars.xw_empty[s % kStXw]);
                 mma_commit(&bars.b_done[st]);
                 // the builders consumed x(s) before xw_full
@@ -1846,7 +1818,11 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
                 const uint32_t off = sw128_off(j, c);
                 const float wj = wv[j];
                 uint4 hi, lo;
-                split_xw8(*reinterpret_cast<const uint4*>(x + off), f2_of(wj, wj), hi, lo);
+                if constexpr (X3)
+                    split_xw8_x3(*reinterpret_cast<const uint4*>(x + off), *reinterpret_cast<const uint4*>(x + 8192 + off),
+                                 f2_of(wj, wj), hi, lo);
+                else
+                    split_xw8(*reinterpret_cast<const uint4*>(x + off), f2_of(wj, wj), hi, lo);
                 *reinterpret_cast<uint4*>(xh + off) = hi;
                 *reinterpret_cast<uint4*>(xh + 8192 + off) = lo;
             }
@@ -1892,22 +1868,6 @@ __global__ void __launch_bounds__(kStThreads, kStCtas) tc_state_kernel(const __g
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// 4-D bf16 map (inner, d1, tok, seq) with a 64 x 1 x box_tok x 1 box,
-// 128-byte swizzle.  Coordinates past the extents read as zero.
-bool make_map(EncodeFn fn, CUtensorMap* m, const void* base, int64_t inner, int64_t d1, int64_t tok, int64_t seq,
-              int64_t s1, int64_t s_tok, int64_t s_seq, int box_tok = kCS) {
-    cuuint64_t dims[4] = {(cuuint64_t)inner, (cuuint64_t)d1, (cuuint64_t)tok, (cuuint64_t)seq};
-    cuuint64_t strides[3] = {(cuuint64_t)(s1 * 2), (cuuint64_t)(s_tok * 2), (cuuint64_t)(s_seq * 2)};
-    cuuint32_t box[4] = {64, 1, (cuuint32_t)box_tok, 1};
-    cuuint32_t es[4] = {1, 1, 1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 
 // fp32 y (chan, head, tok, seq) in 32 x 1 x 64 x 1 boxes, no swizzle: the
 // fast output kernel's TMA stores.  When the channel stride is not 1, or a
@@ -1924,14 +1884,18 @@ bool make_y_map(EncodeFn fn, CUtensorMap* m, const ScanParams& p) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Maps of the state kernel: x and B in 64-token boxes (its step).
-bool make_state_maps(EncodeFn fn, TcMaps* m, const ScanParams& p) {
+// Maps of the state kernel: x and B in 64-token boxes (its step); with x3,
+// also their low halves (same strides as the bf16 copies p points at).
+bool make_state_maps(EncodeFn fn, TcMaps* m, const ScanParams& p, bool x3) {
     const int64_t S = p.S;
-    std::memset(&m->c, 0, sizeof(m->c));
-    std::memset(&m->y, 0, sizeof(m->y));
-    m->y_ok = 0;
-    return make_map(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf) &&
-           make_map(fn, &m->b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf);
+    std::memset(m, 0, sizeof(*m));
+    if (!make_map(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf) ||
+        !make_map(fn, &m->b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf))
+        return false;
+    if (!x3) return true;
+    return p.cast_xl && p.cast_bl &&
+           make_map(fn, &m->xl, p.cast_xl, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf) &&
+           make_map(fn, &m->bl, p.cast_bl, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf);
 }
 
 // Test hook: HELIX_TC_GENERAL=1 sends every CTA of the output kernel down
@@ -1948,7 +1912,38 @@ int configure_tc(const helix_ctx*) {
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(tc_out_general_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_OUT);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(tc_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_STATE);
+    e = cudaFuncSetAttribute(tc_state_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_STATE);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(tc_state_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_STATE_X3);
+}
+
+int launch_tc_state_pass(const helix_ctx* ctx, const ScanParams& p, int runs, bool x3, void* stream) {
+    auto fn = reinterpret_cast<EncodeFn>(ctx->encode_tiled);
+    if (!fn) return cudaErrorNotSupported;
+    TcMaps maps;
+    if (!make_state_maps(fn, &maps, p, x3)) return cudaErrorInvalidValue;
+    const int64_t per_run = (int64_t)p.n_pslab * p.H * p.S * p.n_half;
+    const unsigned grid = (unsigned)(per_run * runs);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (x3)
+        tc_state_kernel<true><<<grid, kStThreads, SMEM_STATE_X3, st>>>(maps, p, runs);
+    else
+        tc_state_kernel<false><<<grid, kStThreads, SMEM_STATE, st>>>(maps, p, runs);
+    return cudaGetLastError();
+}
+
+int launch_tc_carry(const ScanParams& p, bool after_ours, void* stream) {
+    const int64_t n4 = (int64_t)p.S * p.H * p.P * p.N / 4;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((n4 + kCarryThreads - 1) / kCarryThreads));
+    cfg.blockDim = dim3(kCarryThreads);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = after_ours ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, tc_carry_kernel, p);
 }
 
 int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void* stream) {
@@ -1974,13 +1969,8 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void
     if (!maps.y_ok) std::memset(&maps.y, 0, sizeof(maps.y));
     const bool do_a = (!only || *only == 'A') && !pl.states_ready;
     const bool do_c = !only || *only == 'C';
-    const int64_t per_run = (int64_t)p.n_pslab * p.H * S * p.n_half;
     if (pl.need_state_kernel && do_a) {
-        const int runs = pl.state_runs;
-        TcMaps smaps;
-        if (!make_state_maps(fn, &smaps, p)) return cudaErrorInvalidValue;
-        tc_state_kernel<<<(unsigned)(per_run * runs), kStThreads, SMEM_STATE, st>>>(smaps, p, runs);
-        const cudaError_t e = cudaGetLastError();
+        const int e = launch_tc_state_pass(ctx, p, pl.state_runs, false, stream);
         if (e != cudaSuccess) return e;
     }
     const bool do_b = !only || *only == 'B';
@@ -2038,13 +2028,7 @@ int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_i
         const int e = launch_cast(ctx, pl, &p, stream, true);
         if (e != cudaSuccess) return e;
     }
-    TcMaps maps;
-    const int64_t S = p.S;
-    if (!make_state_maps(fn, &maps, p)) return cudaErrorInvalidValue;
-    const int64_t per_run = (int64_t)p.n_pslab * p.H * S * p.n_half;
-    tc_state_kernel<<<(unsigned)(per_run * pl.state_runs), kStThreads, SMEM_STATE, static_cast<cudaStream_t>(stream)>>>(
-        maps, p, pl.state_runs);
-    return cudaGetLastError();
+    return launch_tc_state_pass(ctx, p, pl.state_runs, false, stream);
 }
 
 int fault_word_address(unsigned** out) {

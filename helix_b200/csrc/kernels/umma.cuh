@@ -304,6 +304,11 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
     asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -322,6 +327,26 @@ __device__ __forceinline__ void split_xw8(const uint4& x, uint64_t w2, uint4& hi
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         const uint64_t p = f2_mul(f2_of_bf16x2(in[e]), w2);
+        float p0, p1;
+        f2_to(p, p0, p1);
+        h[e] = pack_bf16x2(p0, p1);
+        float l0, l1;
+        f2_to(f2_sub(p, f2_of_bf16x2(h[e])), l0, l1);
+        l[e] = pack_bf16x2(l0, l1);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Same, with x given as a bf16 pair (hi + lo, about 16 significant bits):
+// w (xh + xl) split into hi and lo again.
+__device__ __forceinline__ void split_xw8_x3(const uint4& xh, const uint4& xl, uint64_t w2, uint4& hi, uint4& lo) {
+    const uint32_t a[4] = {xh.x, xh.y, xh.z, xh.w};
+    const uint32_t b[4] = {xl.x, xl.y, xl.z, xl.w};
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const uint64_t p = f2_mul(f2_add(f2_of_bf16x2(a[e]), f2_of_bf16x2(b[e])), w2);
         float p0, p1;
         f2_to(p, p0, p1);
         h[e] = pack_bf16x2(p0, p1);

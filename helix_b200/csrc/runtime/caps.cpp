@@ -48,18 +48,24 @@ size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 }  // namespace
 
 // Precision selects the kernel family:
-//   backend REF or SGMMA          -> exact fp32 (the reference's fp32 paths)
-//   backend MPP                   -> tcgen05 bf16 (the reference's bf16 path)
-//   backend AUTO                  -> compute_dtype decides
-//   F32-stored x, B, C on the tcgen05 family need scratch for their bf16
-//   copies, so single pass takes the fp32 family (as the reference's bf16
-//   Pass C needs its multipass staging, src/runtime/caps.mm:59-72)
+//   backend REF                   -> exact fp32 on CUDA cores (the reference's
+//                                    scalar path for differential testing)
+//   backend SGMMA, or AUTO with   -> tcgen05 three-product family: fp32
+//   compute_dtype F32                operands as bf16 hi + lo pairs, products
+//                                    hi.hi + hi.lo + lo.hi, fp32 accumulators
+//                                    and state (the reference's fp32 matrix
+//                                    path, src/runtime/caps.mm:19, 97-102)
+//   backend MPP, or AUTO with     -> tcgen05 bf16 (the reference's bf16 path)
+//   compute_dtype BF16
+// The tcgen05 families read F32-stored x, B, C through copies in the scratch,
+// so single pass (no scratch) takes the exact fp32 family, as does the
+// three-product family's request with bf16-stored x, B, C (the reference's
+// bf16 Pass C needs its multipass staging too, src/runtime/caps.mm:59-72).
 Path select_path(const helix_scan_desc& d) {
-    if (d.backend == HELIX_BACKEND_REF || d.backend == HELIX_BACKEND_SGMMA) return kPathSimtF32;
-    const bool tc = d.backend == HELIX_BACKEND_MPP || d.compute_dtype == HELIX_BF16;
-    if (!tc) return kPathSimtF32;
-    if (d.io_dtype == HELIX_F32 && !d.multipass) return kPathSimtF32;
-    return kPathTcBf16;
+    if (d.backend == HELIX_BACKEND_REF) return kPathSimtF32;
+    const bool bf16 = d.backend == HELIX_BACKEND_MPP || (d.backend != HELIX_BACKEND_SGMMA && d.compute_dtype == HELIX_BF16);
+    if (bf16) return d.io_dtype == HELIX_F32 && !d.multipass ? kPathSimtF32 : kPathTcBf16;
+    return d.io_dtype == HELIX_F32 && d.multipass ? kPathTcX3 : kPathSimtF32;
 }
 
 bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why) {
@@ -91,8 +97,15 @@ bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why) 
         return true;
     }
 
-    // tcgen05 path.
+    // tcgen05 paths.
     if (!ctx->tc_ready) return no("tensor-core kernels unavailable on this device");
+    if (select_path(d) == kPathTcX3) {
+        // 128 states per pass (two passes above 128), B and C read through
+        // their bf16 copies by TMA: rows of d_state * 2 bytes, multiple of 16
+        if (d.d_state % 8 != 0 || d.d_state > 256)
+            return no("tensor-core fp32 path needs d_state % 8 == 0 and <= 256");
+        return true;
+    }
     // 128 states per pass of the kernels (two passes above 128); rows of B
     // and C are TMA-loaded, so d_state * 2 bytes must be a multiple of 16.
     if (d.d_state % 8 != 0 || d.d_state > 256)
@@ -109,15 +122,17 @@ bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why) 
 
 namespace {
 
-// Run cut of the tensor-core family.  Its output kernel gives a CTA two
-// 64-channel slabs of one group (a "pair") over a span of consecutive runs,
-// so the span length is picked first: the one that minimises (waves of
+// Run cut of the tensor-core families.  Their output kernels give a CTA
+// slabs_per_cta 64-channel slabs of one group (bf16: a "pair" of two; the
+// three-product family: one) over a span of consecutive runs, so the span
+// length is picked first: the one that minimises (waves of
 // CTAs) x (blocks per span + half a block of start-up).  The span is then
-// cut into runs fine enough that the state kernel (two CTAs per SM) has
-// about four CTAs per SM to spread over.
-void tc_split(const helix_scan_desc& d, int blocks, int n_sm, int max_runs, int* run_blocks, int* out_k) {
+// cut into runs fine enough that the state kernel (state_ctas CTAs per SM)
+// has enough CTAs to spread over.
+void tc_split(const helix_scan_desc& d, int blocks, int n_sm, int max_runs, int slabs_per_cta, int state_ctas,
+              int* run_blocks, int* out_k) {
     const int64_t units = (int64_t)(d.n_head / d.n_group) * ((d.head_dim + kSlab - 1) / kSlab);
-    const int64_t pairs = (int64_t)d.n_seq * d.n_group * ((units + 1) / 2);
+    const int64_t pairs = (int64_t)d.n_seq * d.n_group * ((units + slabs_per_cta - 1) / slabs_per_cta);
     double best = 1e300;
     int sb = blocks;
     for (int n = 1; n <= blocks; ++n) {
@@ -134,12 +149,12 @@ void tc_split(const helix_scan_desc& d, int blocks, int n_sm, int max_runs, int*
     int k = 1;
     if (n_out > 1) {
         // Runs per span for the state kernel: each CTA reduces one run of one
-        // slab, kStateCtasPerSm CTAs share an SM, and a CTA costs about
+        // slab, state_ctas CTAs share an SM, and a CTA costs about
         // kStateStartSteps 64-token steps of set-up on top of two steps per
         // 128-token block.  Pick the divisor of the span that minimises
         // waves x per-CTA steps, within the run-slot budget.
         const int64_t st_units = (int64_t)d.n_seq * d.n_head * ((d.head_dim + kSlab - 1) / kSlab) * (n_out - 1);
-        const int64_t slots = (int64_t)kStateCtasPerSm * n_sm;
+        const int64_t slots = (int64_t)state_ctas * n_sm;
         double kbest = 1e300;
         for (int c = 1; c <= sb; ++c) {
             if (sb % c != 0) continue;
@@ -177,7 +192,8 @@ void lay_out_scratch(const helix_scan_desc& d, Plan* pl) {
     add_cast_regions(d, pl);
 }
 
-// The bf16 copies of F32-stored x, B, C at the end of the scratch.
+// The bf16 copies of F32-stored x, B, C at the end of the scratch (and their
+// low halves for the three-product family).
 void add_cast_regions(const helix_scan_desc& d, Plan* pl) {
     if (!pl->cast) return;
     pl->x_pitch = (d.head_dim + 7) / 8 * 8;
@@ -186,6 +202,11 @@ void add_cast_regions(const helix_scan_desc& d, Plan* pl) {
     pl->off_bc = pl->off_xc + align256(rows * d.n_head * pl->x_pitch * 2);
     pl->off_cc = pl->off_bc + align256(rows * d.n_group * d.d_state * 2);
     pl->total = pl->off_cc + align256(rows * d.n_group * d.d_state * 2);
+    if (!pl->cast_lo) return;
+    pl->off_xl = pl->total;
+    pl->off_bl = pl->off_xl + align256(rows * d.n_head * pl->x_pitch * 2);
+    pl->off_cl = pl->off_bl + align256(rows * d.n_group * d.d_state * 2);
+    pl->total = pl->off_cl + align256(rows * d.n_group * d.d_state * 2);
 }
 
 }  // namespace
@@ -193,7 +214,8 @@ void add_cast_regions(const helix_scan_desc& d, Plan* pl) {
 Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     Plan pl;
     pl.path = select_path(d);
-    pl.cs = pl.path == kPathTcBf16 ? 128 : (d.d_state <= 128 ? 64 : 32);
+    const bool tc = pl.path == kPathTcBf16 || pl.path == kPathTcX3;
+    pl.cs = tc ? 128 : (d.d_state <= 128 ? 64 : 32);
     pl.n_pslab = (d.head_dim + kSlab - 1) / kSlab;
 
     const int blocks = (d.n_tok + kRunQuantum - 1) / kRunQuantum;  // 128-token blocks
@@ -206,7 +228,9 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
         if (const int f = forced_run_tokens()) {
             run_blocks = std::max(1, f / kRunQuantum);
         } else if (pl.path == kPathTcBf16) {
-            tc_split(d, blocks, n_sm, max_runs, &run_blocks, &out_k);
+            tc_split(d, blocks, n_sm, max_runs, 2, kStateCtasPerSm, &run_blocks, &out_k);
+        } else if (pl.path == kPathTcX3) {
+            tc_split(d, blocks, n_sm, max_runs, 1, kStateCtasPerSmX3, &run_blocks, &out_k);
         } else {
             // Enough CTAs in the output kernel to cover every SM a few times.
             const int64_t units = (int64_t)d.n_seq * d.n_head * pl.n_pslab;
@@ -231,7 +255,8 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     // ... and, when a state pass runs, the largest decay span of every run's
     // chunks, measured there, so the output kernel need not read dt for it.
     pl.has_span = pl.has_flags && pl.need_state_kernel;
-    pl.cast = d.multipass && pl.path == kPathTcBf16 && d.io_dtype == HELIX_F32;
+    pl.cast = d.multipass && ((pl.path == kPathTcBf16 && d.io_dtype == HELIX_F32) || pl.path == kPathTcX3);
+    pl.cast_lo = pl.path == kPathTcX3;
     lay_out_scratch(d, &pl);
     return pl;
 }
@@ -269,15 +294,19 @@ extern "C" size_t helix_scan_scratch_size(helix_ctx* ctx, const helix_scan_desc*
 extern "C" helix_backend helix_ctx_select_backend(helix_ctx* ctx, const helix_scan_desc* d) {
     if (!ctx || !d) return HELIX_BACKEND_REF;
     if (d->backend == HELIX_BACKEND_REF) return HELIX_BACKEND_REF;
-    return hx::select_path(*d) == hx::kPathTcBf16 ? HELIX_BACKEND_MPP : HELIX_BACKEND_SGMMA;
+    if (!hx::supported_impl(ctx, *d, nullptr)) return HELIX_BACKEND_REF;
+    const hx::Path path = hx::select_path(*d);
+    return path == hx::kPathTcBf16 ? HELIX_BACKEND_MPP : path == hx::kPathTcX3 ? HELIX_BACKEND_SGMMA : HELIX_BACKEND_REF;
 }
 
 extern "C" const char* helix_ctx_backend_desc(helix_ctx* ctx, const helix_scan_desc* d) {
     if (!ctx || !d) return "unavailable (null context)";
     if (!hx::supported_impl(ctx, *d, nullptr)) return "declined (shape unsupported)";
-    return hx::select_path(*d) == hx::kPathTcBf16
-               ? "tcgen05 (bf16 operands, fp32 accumulators and state)"
-               : "cuda-core (fp32)";
+    switch (hx::select_path(*d)) {
+        case hx::kPathTcBf16: return "tcgen05 (bf16 operands, fp32 accumulators and state)";
+        case hx::kPathTcX3: return "tcgen05 (fp32 operands as bf16 hi+lo, three products, fp32 accumulators and state)";
+        default: return "cuda-core (exact fp32)";
+    }
 }
 
 extern "C" helix_status helix_scan_plan_info(helix_ctx* ctx, const helix_scan_desc* d, helix_plan_info* out) {
@@ -288,7 +317,7 @@ extern "C" helix_status helix_scan_plan_info(helix_ctx* ctx, const helix_scan_de
         return HELIX_ERR_UNSUPPORTED_SHAPE;
     }
     const hx::Plan pl = hx::make_plan(ctx, *d);
-    out->family = pl.path == hx::kPathTcBf16 ? 1 : 0;
+    out->family = (int32_t)pl.path;
     out->chunk = pl.cs;
     out->run_tokens = pl.run_tok;
     out->n_runs = pl.n_runs;

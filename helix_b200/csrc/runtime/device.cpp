@@ -104,7 +104,7 @@ extern "C" helix_status helix_ctx_create(helix_ctx** out, void* device, const ch
             delete ctx;
             return HELIX_ERR_PIPELINE;
         }
-        ctx->tc_ready = hx::configure_tc(ctx) == cudaSuccess;
+        ctx->tc_ready = hx::configure_tc(ctx) == cudaSuccess && hx::configure_tc3(ctx) == cudaSuccess;
         if (!ctx->tc_ready) cudaGetLastError();
         if (hx::fault_word_address(&ctx->fault_word) != cudaSuccess) {
             cudaGetLastError();

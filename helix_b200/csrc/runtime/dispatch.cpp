@@ -159,13 +159,20 @@ void bind_scratch(const Plan& pl, char* base, ScanParams* p) {
         p->cast_b = base + pl.off_bc;
         p->cast_c = base + pl.off_cc;
     }
+    if (pl.cast_lo) {
+        p->cast_xl = base + pl.off_xl;
+        p->cast_bl = base + pl.off_bl;
+        p->cast_cl = base + pl.off_cl;
+    }
 }
 
 helix_status run_call(helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream) {
     int dev_prev = -1;
     cudaGetDevice(&dev_prev);
     if (dev_prev != ctx->device) cudaSetDevice(ctx->device);
-    const int rc = pl.path == kPathTcBf16 ? launch_tc(ctx, pl, p, stream) : launch_simt(ctx, pl, p, stream);
+    const int rc = pl.path == kPathTcBf16 ? launch_tc(ctx, pl, p, stream)
+                   : pl.path == kPathTcX3 ? launch_tc3(ctx, pl, p, stream)
+                                          : launch_simt(ctx, pl, p, stream);
     if (dev_prev >= 0 && dev_prev != ctx->device) cudaSetDevice(dev_prev);
     if (rc != cudaSuccess) {
         set_error(ctx, std::string("kernel launch failed: ") + cudaGetErrorString(static_cast<cudaError_t>(rc)));

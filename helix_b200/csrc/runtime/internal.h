@@ -37,11 +37,14 @@ constexpr int kMaxRuns = 256;
 // Tensor-core state kernel: CTAs resident per SM, and its fixed cost per CTA
 // (first loads, first decay weights, drain) in 64-token steps, as measured.
 constexpr int kStateCtasPerSm = 3;
+constexpr int kStateCtasPerSmX3 = 2;  // three-product family (larger rings)
 constexpr double kStateStartSteps = 3.5;
 
 enum Path : int {
     kPathSimtF32 = 0,   // exact fp32 CUDA-core kernels
     kPathTcBf16  = 1,   // tcgen05 kernels, bf16 operands, fp32 state
+    kPathTcX3    = 2,   // tcgen05 kernels, three-product bf16 split of fp32
+                        // operands (hi.hi + hi.lo + lo.hi), fp32 state
 };
 
 // How one descriptor is executed.  A pure function of (ctx, desc, env):
@@ -74,6 +77,11 @@ struct Plan {
     size_t off_xc   = 0;    // bf16 [seq][tok][head][x_pitch]
     size_t off_bc   = 0;    // bf16 [seq][tok][group][d_state]
     size_t off_cc   = 0;    // bf16 [seq][tok][group][d_state]
+    // Three-product family: the low halves of the copies, same layouts.
+    bool   cast_lo  = false;
+    size_t off_xl   = 0;
+    size_t off_bl   = 0;
+    size_t off_cl   = 0;
     size_t total    = 0;    // scratch bytes
     // The run states (and bf16 copies) are already in the scratch, left by
     // helix_scan_shard_state: no cast and no state kernel run.
@@ -123,6 +131,9 @@ struct ScanParams {
     void*          cast_x;      // scratch: bf16 copies (Plan::cast), else null
     void*          cast_b;
     void*          cast_c;
+    void*          cast_xl;     // scratch: their low halves (Plan::cast_lo), else null
+    void*          cast_bl;
+    void*          cast_cl;
 
     unsigned*      fault;       // the device fault word (helix_device_fault)
     int64_t        s_row_bytes; // bytes one s0 / s1 row spans
@@ -188,9 +199,17 @@ bool states_overlap(const helix_scan_desc& d, const void* s0, const void* s1);
 // Kernel launchers (kernels/*.cu).  Return cudaSuccess or the launch error.
 int launch_simt(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+int launch_tc3(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 // State kernel over every run of the plan (p.agg / p.lam for all n_runs).
 int launch_simt_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+int launch_tc3_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+// kernels/scan_tc.cu, shared with scan_tc3.cu: the tcgen05 state kernel over
+// `runs` runs (x3: the three-product mode, reading the low halves from
+// p.cast_xl / p.cast_bl), and the carry kernel (programmatic dependent of
+// the previous kernel when after_ours).
+int launch_tc_state_pass(const helix_ctx* ctx, const ScanParams& p, int runs, bool x3, void* stream);
+int launch_tc_carry(const ScanParams& p, bool after_ours, void* stream);
 // kernels/scan_cast.cu: when `run`, enqueues the bf16 copies of x, B, C into
 // p->cast_*; then points *p at the copies (dense strides, io_bf16 = 1).
 int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* stream, bool run);
@@ -206,6 +225,7 @@ int launch_carry_combine(const ScanParams& p, const float* states, const float* 
                          float* carry, void* stream);
 int configure_simt(const helix_ctx* ctx);
 int configure_tc(const helix_ctx* ctx);
+int configure_tc3(const helix_ctx* ctx);
 int read_tc_fault(unsigned* code);
 // Device address of the fault word on the current device.
 int fault_word_address(unsigned** out);

@@ -94,6 +94,7 @@ extern "C" helix_status helix_scan_shard_state(helix_ctx* ctx, void* stream, con
     }
     DeviceScope ds(ctx->device);
     int rc = pl.path == hx::kPathTcBf16 ? hx::launch_tc_states(ctx, pl, p, stream)
+             : pl.path == hx::kPathTcX3 ? hx::launch_tc3_states(ctx, pl, p, stream)
                                         : hx::launch_simt_states(ctx, pl, p, stream);
     if (rc == cudaSuccess) rc = hx::launch_shard_fold(p, at<float>(state), at<float>(log_decay), stream);
     if (rc != cudaSuccess) return launch_error(ctx, rc);

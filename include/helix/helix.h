@@ -76,13 +76,17 @@ typedef enum {
 } helix_a_form;
 
 typedef enum {
-    /* The names are kept for ABI compatibility.  On B200 the kernel variant is
-     * chosen by compute_dtype:
-     *   compute_dtype F32  -> exact fp32 CUDA-core kernels
-     *   compute_dtype BF16 -> tcgen05 tensor-core kernels (bf16 operands,
-     *                         fp32 accumulators, fp32 carried state)
-     * AUTO, SGMMA and MPP all resolve to that choice.  REF is accepted and
-     * always runs the exact fp32 kernels, for differential testing. */
+    /* The names are kept for ABI compatibility.  On B200:
+     *   MPP, or AUTO with compute_dtype BF16
+     *       -> tcgen05 kernels, bf16 operands (F32-stored x, B, C rounded
+     *          once), fp32 accumulators and carried state
+     *   SGMMA, or AUTO with compute_dtype F32
+     *       -> tcgen05 kernels at fp32-class accuracy: every fp32 operand as
+     *          a bf16 pair hi + lo, each product as hi.hi + hi.lo + lo.hi,
+     *          fp32 accumulators and carried state (F32-stored x, B, C,
+     *          multipass; otherwise the exact kernels below run)
+     *   REF -> exact fp32 CUDA-core kernels, for differential testing
+     * (also the family for single pass with F32-stored x, B, C). */
     HELIX_BACKEND_AUTO  = 0,
     HELIX_BACKEND_SGMMA = 1,
     HELIX_BACKEND_MPP   = 2,

@@ -64,7 +64,8 @@ helix_status helix_scan_encode_static(helix_ctx*             ctx,
  * HELIX_ERR_UNSUPPORTED_SHAPE (and fills nothing) for a descriptor
  * helix_scan_supported rejects. */
 typedef struct helix_plan_info {
-    int32_t  family;         /* 0: fp32 CUDA-core kernels, 1: tcgen05 bf16 kernels */
+    int32_t  family;         /* 0: exact fp32 CUDA-core kernels, 1: tcgen05 bf16,
+                                2: tcgen05 three-product (fp32-class) */
     int32_t  chunk;          /* tokens per chunk of the output kernel */
     int32_t  run_tokens;     /* tokens per run */
     int32_t  n_runs;         /* runs per sequence */

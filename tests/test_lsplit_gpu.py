@@ -17,16 +17,22 @@ import socket
 import numpy as np
 import pytest
 
-from gpu_harness import BF16_ABS, BF16_REL, BF16_RL2, F32_ABS, F32_REL, F32_RL2, record, widen
+from gpu_harness import (BF16_ABS, BF16_REL, BF16_RL2, F32_ABS, F32_REL, F32_RL2, X3_ABS, X3_REL, X3_RL2, record,
+                         widen)
 from helpers import compare
 from helix_b200 import abi
 
 pytestmark = pytest.mark.gpu
 
-# state bounds: fp32 path as the fp32 parity tests; bf16 path as the bf16
-# parity tests' carried-state bound (hi/lo split state update)
-ST_BOUNDS = {"f32": (F32_REL, F32_ABS, F32_RL2), "bf16": (2e-5, 2e-6, 1e-4)}
-Y_BOUNDS = {"f32": (F32_REL, F32_ABS, F32_RL2), "bf16": (BF16_REL, BF16_ABS, BF16_RL2)}
+# "io" cases: F32-stored inputs on the fp32-class tensor-core family (the
+# default for compute F32), on the exact CUDA-core family (backend REF), and
+# bf16-stored inputs on the bf16 family.  State bounds: the fp32 parity
+# suites'; the bf16 parity tests' carried-state bound (hi/lo split update).
+ST_BOUNDS = {"f32": (X3_REL, X3_ABS, X3_RL2), "f32-exact": (F32_REL, F32_ABS, F32_RL2), "bf16": (2e-5, 2e-6, 1e-4)}
+Y_BOUNDS = {"f32": (X3_REL, X3_ABS, X3_RL2), "f32-exact": (F32_REL, F32_ABS, F32_RL2),
+            "bf16": (BF16_REL, BF16_ABS, BF16_RL2)}
+BACKEND = {"f32": abi.HELIX_BACKEND_AUTO, "f32-exact": abi.HELIX_BACKEND_REF, "bf16": abi.HELIX_BACKEND_AUTO}
+IOS = ["f32", "f32-exact", "bf16"]
 
 
 def _torch(prob, io, dev="cuda:0"):
@@ -68,7 +74,7 @@ SHAPES = [(300, 2, 4, 64, 128, 2), (1024, 1, 8, 64, 128, 8), (129, 3, 2, 72, 128
 
 
 @pytest.mark.parametrize("runs", [None, "128"], ids=["auto-runs", "runs128"])
-@pytest.mark.parametrize("io", ["f32", "bf16"])
+@pytest.mark.parametrize("io", IOS)
 @pytest.mark.parametrize("shape", SHAPES, ids=["L{}S{}H{}P{}N{}G{}".format(*s) for s in SHAPES])
 @pytest.mark.parametrize("long_mem", [False, True], ids=["short", "long"])
 def test_shard_state(ctx, oracle, run_tokens, shape, io, runs, long_mem):
@@ -80,7 +86,7 @@ def test_shard_state(ctx, oracle, run_tokens, shape, io, runs, long_mem):
     _, s_ref = oracle.scan(d, np.zeros_like(prob["s0"]), prob["x"], prob["dt"], prob["A"], prob["B"], prob["C"])
     t = _torch(prob, io)
     run_tokens(runs)
-    state, ld = helix_b200.shard_state(t["x"], t["dt"], t["A"], t["B"], t["C"], ctx=ctx)
+    state, ld = helix_b200.shard_state(t["x"], t["dt"], t["A"], t["B"], t["C"], ctx=ctx, backend=BACKEND[io])
     torch.cuda.synchronize()
     _check(f"shard_state {io} {shape}", state.cpu().numpy(), s_ref, ST_BOUNDS[io])
     np.testing.assert_allclose(ld.cpu().numpy(), _log_decay(prob, d), rtol=2e-5, atol=1e-4)
@@ -110,7 +116,7 @@ def test_carry_combine(ctx, n_prev, with_ids):
 
 
 @pytest.mark.parametrize("via", ["scan", "scan_shard"])
-@pytest.mark.parametrize("io", ["f32", "bf16"])
+@pytest.mark.parametrize("io", IOS)
 @pytest.mark.parametrize("cuts", [(0, 512, 1024), (0, 100, 613, 640, 1024)], ids=["2shards", "4shards-ragged"])
 def test_lsplit_emulated_on_one_gpu(ctx, oracle, run_tokens, io, cuts, via):
     """K token shards of one problem on one GPU: shard states, carry
@@ -129,8 +135,9 @@ def test_lsplit_emulated_on_one_gpu(ctx, oracle, run_tokens, io, cuts, via):
     shards = [(a, b) for a, b in zip(cuts[:-1], cuts[1:])]
     sl = lambda k, a, b: t[k][:, a:b].contiguous()
     run_tokens("128")  # several runs per shard: the run states carry
+    be = BACKEND[io]
     pairs = [helix_b200.shard_state(sl("x", a, b), sl("dt", a, b), t["A"], sl("B", a, b), sl("C", a, b), ctx=ctx,
-                                    keep_scratch=True)
+                                    keep_scratch=True, backend=be)
              for a, b in shards]
     states = torch.stack([p[0] for p in pairs]).contiguous()
     lds = torch.stack([p[1] for p in pairs]).contiguous()
@@ -139,10 +146,10 @@ def test_lsplit_emulated_on_one_gpu(ctx, oracle, run_tokens, io, cuts, via):
         carry = helix_b200.carry_combine(t["s0"], states[:k].contiguous(), lds[:k].contiguous(), ctx=ctx)
         if via == "scan":
             y, s_last = helix_b200.scan(sl("x", a, b), sl("dt", a, b), t["A"], sl("B", a, b), sl("C", a, b),
-                                        carry, ctx=ctx)
+                                        carry, ctx=ctx, backend=be)
         else:
             y, s_last = helix_b200.scan_shard(sl("x", a, b), sl("dt", a, b), t["A"], sl("B", a, b),
-                                              sl("C", a, b), carry, pairs[k][2], ctx=ctx)
+                                              sl("C", a, b), carry, pairs[k][2], ctx=ctx, backend=be)
         ys.append(y)
     torch.cuda.synchronize()
     y = torch.cat(ys, dim=1).cpu().numpy()

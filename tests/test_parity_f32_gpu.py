@@ -1,5 +1,6 @@
-"""GPU parity of the exact-fp32 kernels (backend SGMMA/REF, compute F32)
-against the fp64 oracle, through the C ABI.
+"""GPU parity of the exact-fp32 CUDA-core kernels (backend REF) against the
+fp64 oracle, through the C ABI.  (The fp32-class tensor-core family, backend
+SGMMA / AUTO, has its own suite: test_parity_x3_gpu.py.)
 
 Mirrors reference tests/test_metal_parity.mm: its 22-shape matrix
 (:77-104) x {single pass, multipass, multipass with many runs} x {SHORT, LONG}
@@ -65,8 +66,8 @@ def test_parity_f32(ctx, oracle, run_tokens, shape, mode, long_mem):
     d = oracle.desc_init(L, S, H, P, N, G)
     y_ref, s_ref = oracle.scan(d, *[prob[k] for k in ("s0", "x", "dt", "A", "B", "C")])
     run_tokens(rt)
-    y, s1, dd = run(ctx, prob, multipass=multipass, backend=abi.HELIX_BACKEND_SGMMA)
-    assert ctx.select_backend(dd) == abi.HELIX_BACKEND_SGMMA
+    y, s1, dd = run(ctx, prob, multipass=multipass, backend=abi.HELIX_BACKEND_REF)
+    assert ctx.select_backend(dd) == abi.HELIX_BACKEND_REF
     _check(f"f32 {name} {'long' if long_mem else 'short'} {shape}", y, s1, y_ref, s_ref)
 
 
@@ -97,5 +98,5 @@ def test_baseline_configs_f32(ctx, oracle, cfg):
     d = oracle.desc_init(sh.L, sh.S, sh.H, sh.P, sh.N, sh.G)
     y_ref, s_ref = oracle.scan_mt(d, *[prob[k] for k in ("s0", "x", "dt", "A", "B", "C")],
                                   threads=os.cpu_count() or 1)
-    y, s1, _ = run(ctx, prob, multipass=True, compute="f32")
+    y, s1, _ = run(ctx, prob, multipass=True, compute="f32", backend=abi.HELIX_BACKEND_REF)
     _check(f"baseline {cfg}", y, s1, y_ref, s_ref)

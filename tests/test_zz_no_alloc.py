@@ -29,7 +29,7 @@ import pytest
 import torch
 
 import helix_b200
-from gpu_harness import BF16_ABS, BF16_REL, BF16_RL2, F32_ABS, F32_REL, F32_RL2, widen
+from gpu_harness import BF16_ABS, BF16_REL, BF16_RL2, X3_ABS, X3_REL, X3_RL2, widen
 from helpers import compare
 from helix_b200 import abi
 
@@ -88,8 +88,8 @@ def _check_call(ctx, oracle, prob, shape, compute, tag):
     y_ref, s_ref = oracle.scan(od, *[w[k] for k in ("s0", "x", "dt", "A", "B", "C")])
     if compute == "bf16":
         yb, sb = (BF16_REL, BF16_ABS, BF16_RL2), S1_BF16
-    else:
-        yb = sb = (F32_REL, F32_ABS, F32_RL2)
+    else:  # compute F32 on F32-stored inputs: the fp32-class tensor-core family
+        yb = sb = (X3_REL, X3_ABS, X3_RL2)
     got = dict(y=y.cpu().numpy(), s1=s1.cpu().numpy())
     enc = dict(y=y_enc.cpu().numpy(), s1=s_enc.cpu().numpy())
     for name, want, (rel, abs_, rl2) in (("y", y_ref, yb), ("s1", s_ref, sb)):
