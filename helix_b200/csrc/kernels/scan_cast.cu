@@ -103,6 +103,52 @@ __global__ void __launch_bounds__(kCastThreads) cast_bf16_kernel(ScanParams p, C
     }
 }
 
+// Dense sources (the common case): x, B and C as flat arrays whose copies
+// have the same element order.  Eight elements per thread step, two steps in
+// flight per thread: the kernel is a stream of 16-byte loads and stores.
+struct FlatSeg {
+    const float* src;
+    __nv_bfloat16* hi;
+    __nv_bfloat16* lo;  // null: no low halves
+    int64_t n8;         // groups of eight elements
+};
+struct FlatCast {
+    FlatSeg seg[3];
+};
+
+__device__ __forceinline__ void cast8(const FlatSeg& g, int64_t k) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(g.src) + 2 * k);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(g.src) + 2 * k + 1);
+    const uint2 h0 = bf16x4(a.x, a.y, a.z, a.w), h1 = bf16x4(b.x, b.y, b.z, b.w);
+    reinterpret_cast<uint4*>(g.hi)[k] = make_uint4(h0.x, h0.y, h1.x, h1.y);
+    if (g.lo) {
+        auto res = [](float v, uint32_t w, bool high) { return v - __uint_as_float(high ? (w & 0xffff0000u) : (w << 16)); };
+        const uint2 l0 = bf16x4(res(a.x, h0.x, false), res(a.y, h0.x, true), res(a.z, h0.y, false), res(a.w, h0.y, true));
+        const uint2 l1 = bf16x4(res(b.x, h1.x, false), res(b.y, h1.x, true), res(b.z, h1.y, false), res(b.w, h1.y, true));
+        reinterpret_cast<uint4*>(g.lo)[k] = make_uint4(l0.x, l0.y, l1.x, l1.y);
+    }
+}
+
+__global__ void __launch_bounds__(kCastThreads) cast_flat_kernel(FlatCast f) {
+    const int64_t n0 = f.seg[0].n8, n1 = n0 + f.seg[1].n8, total = n1 + f.seg[2].n8;
+    const int64_t stride = (int64_t)gridDim.x * kCastThreads;
+    for (int64_t q = (int64_t)blockIdx.x * kCastThreads + threadIdx.x; q < total; q += 2 * stride) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int64_t k = q + u * stride;
+            if (k >= total) break;
+            if (k < n0)
+                cast8(f.seg[0], k);
+            else if (k < n1)
+                cast8(f.seg[1], k - n0);
+            else
+                cast8(f.seg[2], k - n1);
+        }
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 }  // namespace
 
 int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* stream, bool run) {
@@ -114,7 +160,26 @@ int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* strea
     d.bl = static_cast<__nv_bfloat16*>(p->cast_bl);
     d.cl = static_cast<__nv_bfloat16*>(p->cast_cl);
     d.pp = pl.x_pitch;
-    if (run) {
+    // dense x (copy pitch = head_dim), B and C, all 16-byte aligned: flat copies
+    const bool x_flat = p->s_x2 == 1 && d.pp == p->P && p->s_x1 == p->P && p->s_x0 == (int64_t)p->H * p->P &&
+                        p->seq_x == (int64_t)p->L * p->H * p->P && aligned16(p->x);
+    const int64_t row_bc = (int64_t)p->G * p->N;
+    const bool bc_flat = p->s_b1 == p->N && p->s_b0 == row_bc && p->seq_b == (int64_t)p->L * row_bc &&
+                         p->s_c1 == p->N && p->s_c0 == row_bc && p->seq_c == (int64_t)p->L * row_bc &&
+                         aligned16(p->B) && aligned16(p->C);
+    if (run && x_flat && bc_flat) {
+        FlatCast f;
+        f.seg[0] = {static_cast<const float*>(p->x), d.x, d.xl, (int64_t)p->S * p->L * p->H * p->P / 8};
+        f.seg[1] = {static_cast<const float*>(p->B), d.b, d.bl, (int64_t)p->S * p->L * row_bc / 8};
+        f.seg[2] = {static_cast<const float*>(p->C), d.c, d.cl, (int64_t)p->S * p->L * row_bc / 8};
+        const int64_t groups = f.seg[0].n8 + f.seg[1].n8 + f.seg[2].n8;
+        const int64_t want = (groups + 2 * kCastThreads - 1) / (2 * kCastThreads);
+        const int64_t cap = (int64_t)(ctx ? ctx->n_sm : 148) * 8;
+        const unsigned grid = (unsigned)(want < cap ? (want > 0 ? want : 1) : cap);
+        cast_flat_kernel<<<grid, kCastThreads, 0, static_cast<cudaStream_t>(stream)>>>(f);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    } else if (run) {
         const int64_t quads = (int64_t)p->S * p->L * (p->H * (d.pp / 4) + 2 * p->G * (p->N / 4));
         const int64_t want = (quads + kCastThreads - 1) / kCastThreads;
         const int64_t cap = (int64_t)(ctx ? ctx->n_sm : 148) * 8;  // grid-stride beyond 8 CTAs per SM

@@ -34,16 +34,22 @@
 // (bounded, see the vector warp), so no decay span needs a second path.
 // Each GEMM is three passes of eight 128 x N x 16 MMAs.
 //
-// Warps (18, 112 registers per thread):
+// Warps (22, 88 registers per thread):
 //   0-3    W_y   y = D2 + e^Lc D3 -> global (one token row per thread)
-//   4-7    W_m   M from D1 -> TMEM (one row per thread)
-//   8-11   W_c   S_next in TMEM (fp32) and its hi | lo copy in smem for G3
-//   12-15  W_b   B' = w B in place, re-split into hi | lo
-//   16     TMA producer and MMA issuer (lane 0)
-//   17     chunk vectors (dt, Lc, w, split decays) into a 3-slot ring
+//   4-7    W_m   M from D1 -> TMEM, tokens j 0-63 of each row (one row per thread)
+//   16-19  W_m   the same, tokens j 64-127
+//   8-11   W_c   half of B' = w B (in place, re-split into hi | lo), then
+//                S_next in TMEM (fp32) and its hi | lo copy in smem for G3
+//   12-15  W_b   the other half of B'
+//   20     TMA producer and MMA issuer (lane 0)
+//   21     chunk vectors (dt, Lc, w, split decays) into a 3-slot ring
+// (two warps of every role but W_y's share each SM sub-partition with warps
+// of other roles, so a role's work on the critical path is spread over all
+// four issue units).
 //
-// MMA issue order per chunk: G1, G3, G4, G2; then C(i+1) once G3 retired,
-// B(i+1) once G4 retired, x(i+1) once G2 retired (one buffer each).
+// MMA issue order per chunk: G1, G3, then G4 and G2 in whichever order their
+// operands (B', M) are ready; then C(i+1) once G3 retired, B(i+1) once G4
+// retired, x(i+1) once G2 retired (one buffer each).
 //
 // TMEM columns: D1 0-127 | M hi 128-191 | M lo 192-255 | D2 256-319 |
 //               D3 320-383 | D4 384-447 | S 448-511.
@@ -68,11 +74,13 @@ namespace {
 using namespace umma;
 using namespace tc;
 
-constexpr int k3Warps = 18;
+constexpr int k3Warps = 22;
 constexpr int k3Threads = 32 * k3Warps;
-constexpr int k3WarpMma = 16, k3WarpVec = 17;
-constexpr int k3RoleThreads = 128;  // W_y, W_m, W_c, W_b: four warps each
-enum Role3 : int { kR3Y = 0, kR3M = 1, kR3C = 2, kR3B = 3 };
+constexpr int k3WarpMma = 20, k3WarpVec = 21;
+enum Role3 : int { kR3Y = 0, kR3M = 1, kR3C = 2, kR3B = 3, kR3Other = 4 };
+__host__ __device__ constexpr int role3_of(int warp) { return warp < 16 ? warp >> 2 : warp < 20 ? kR3M : kR3Other; }
+__host__ __device__ constexpr int role3_threads(int role) { return role == kR3M ? 256 : 128; }
+constexpr int k3BThreads = 256;  // W_b and W_c scale B' together
 
 constexpr int k3Ring = 3;
 constexpr int k3Vec = 4 * 128 + 16;  // floats per ring slot: dt | Lc | w | split dt | flag
@@ -107,9 +115,29 @@ struct Bars3 {
 __device__ __forceinline__ bool role3_wait(const ScanParams& p, uint64_t* bar, uint32_t parity, int role,
                                            unsigned code) {
     const bool ok = mbar_wait(bar, parity, kWaitBudget);
-    const bool all = named_and(1 + role, k3RoleThreads, ok);
-    if (!all && p.fault && (threadIdx.x & (k3RoleThreads - 1)) == 0) atomicCAS(p.fault, 0u, code);
+    const bool all = named_and(1 + role, role3_threads(role), ok);
+    if (!all && p.fault && (threadIdx.x & 127) == 0 && (threadIdx.x >> 5) < 16) atomicCAS(p.fault, 0u, code);
     return all;
+}
+
+// B' = w B of one chunk, in place over the B stage (hi | lo, two 64-state
+// atoms each): thread r of the 256 scaling threads takes every 256th of the
+// 2048 sixteen-byte chunk positions (atom q >> 10, token row (q >> 3) & 127,
+// chunk q & 7), so each quarter warp covers one 128-byte row.
+__device__ __forceinline__ void scale_b(uint8_t* bh, const float* wv, int r) {
+#pragma unroll 4
+    for (int k = 0; k < 2048 / k3BThreads; ++k) {
+        const int q = r + k3BThreads * k;
+        const int j = (q >> 3) & 127;
+        const uint32_t off = (uint32_t)(q >> 10) * 16384u + sw128_off(j, q & 7);
+        const float wj = wv[j];
+        uint4 hi, lo;
+        split_xw8_x3(*reinterpret_cast<const uint4*>(bh + off), *reinterpret_cast<const uint4*>(bh + 32768 + off),
+                     f2_of(wj, wj), hi, lo);
+        *reinterpret_cast<uint4*>(bh + off) = hi;
+        *reinterpret_cast<uint4*>(bh + 32768 + off) = lo;
+    }
+    fence_async_smem();
 }
 __device__ __forceinline__ void warp_arrive3(uint64_t* bar) {
     __syncwarp();
@@ -134,7 +162,7 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
     __shared__ uint32_t tmem_base;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int role = warp >> 2;
+    const int role = role3_of(warp);
     const int row = 32 * (warp & 3) + lane;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
 
@@ -165,15 +193,15 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
         mbar_init(&bars.g4, 1);
         mbar_init(&bars.g2, 1);
         mbar_init(&bars.fin, 1);
-        mbar_init(&bars.d1_read, 4);
-        mbar_init(&bars.m_ready, 4);
-        mbar_init(&bars.b_ready, 4);
+        mbar_init(&bars.d1_read, 8);
+        mbar_init(&bars.m_ready, 8);
+        mbar_init(&bars.b_ready, 8);
         mbar_init(&bars.s_ready, 4);
         mbar_init(&bars.d4_read, 4);
         mbar_init(&bars.d_free, 4);
         for (int k = 0; k < k3Ring; ++k) {
             mbar_init(&bars.v_full[k], 1);
-            mbar_init(&bars.v_empty[k], 16);
+            mbar_init(&bars.v_empty[k], 20);
         }
         fence_mbar_init();
     }
@@ -252,33 +280,49 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
                         mma_bf16(tm + T3_D3, desc_kmajor(a, ks), desc_mnmajor(b, ks), ID3_KM, (pass | ks) != 0);
                 }
                 mma_commit(&bars.g3);
-                // ---- G4(i): D4 = B'^T x ------------------------------------
-                if (!(ok = wait(&bars.x_full, par) && wait(&bars.b_ready, par))) break;
+                // ---- then, each as soon as it can go: G4(i) (B' ready), G2(i)
+                // (M ready), and C(i+1) into the C stage once G3(i) retired
+                if (!(ok = wait(&bars.x_full, par))) break;
                 if (i > 0 && !(ok = wait(&bars.d4_read, par ^ 1u))) break;
-                tc_fence_after();
+                const bool more = i + 1 < n_ch;
+                bool g4_done = false, g2_done = false, c_next = !more;
+                const long long t_start = clock64();
+                while (!(g4_done && g2_done && c_next)) {
+                    if (!g4_done && mbar_try_wait(&bars.b_ready, par)) {
+                        // D4 = B'^T x
+                        tc_fence_after();
 #pragma unroll
-                for (int pass = 0; pass < 3; ++pass) {
-                    const uint32_t a = aB + (pass == 2 ? 32768u : 0u), b = aX + (pass == 1 ? 16384u : 0u);
+                        for (int pass = 0; pass < 3; ++pass) {
+                            const uint32_t a = aB + (pass == 2 ? 32768u : 0u), b = aX + (pass == 1 ? 16384u : 0u);
 #pragma unroll
-                    for (int ks = 0; ks < 8; ++ks)
-                        mma_bf16(tm + T3_D4, desc_mnmajor(a, ks), desc_mnmajor(b, ks), ID3_MM, (pass | ks) != 0);
+                            for (int ks = 0; ks < 8; ++ks)
+                                mma_bf16(tm + T3_D4, desc_mnmajor(a, ks), desc_mnmajor(b, ks), ID3_MM, (pass | ks) != 0);
+                        }
+                        mma_commit(&bars.g4);
+                        g4_done = true;
+                    }
+                    if (!g2_done && mbar_try_wait(&bars.m_ready, par)) {
+                        // D2 = M x
+                        tc_fence_after();
+#pragma unroll
+                        for (int pass = 0; pass < 3; ++pass) {
+                            const uint32_t a = tm + (pass == 2 ? T3_ML : T3_MH), b = aX + (pass == 1 ? 16384u : 0u);
+#pragma unroll
+                            for (int ks = 0; ks < 8; ++ks)
+                                mma_bf16_ts(tm + T3_D2, a + 8 * ks, desc_mnmajor(b, ks), ID3_KM, (pass | ks) != 0);
+                        }
+                        mma_commit(&bars.g2);
+                        g2_done = true;
+                    }
+                    if (!c_next && mbar_try_wait(&bars.g3, par)) {
+                        load_c(i + 1);
+                        c_next = true;
+                    }
+                    if (clock64() - t_start > kWaitBudget) break;
                 }
-                mma_commit(&bars.g4);
-                // ---- G2(i): D2 = M x ---------------------------------------
-                if (!(ok = wait(&bars.m_ready, par))) break;
-                tc_fence_after();
-#pragma unroll
-                for (int pass = 0; pass < 3; ++pass) {
-                    const uint32_t a = tm + (pass == 2 ? T3_ML : T3_MH), b = aX + (pass == 1 ? 16384u : 0u);
-#pragma unroll
-                    for (int ks = 0; ks < 8; ++ks)
-                        mma_bf16_ts(tm + T3_D2, a + 8 * ks, desc_mnmajor(b, ks), ID3_KM, (pass | ks) != 0);
-                }
-                mma_commit(&bars.g2);
-                // ---- the next chunk's operands, each once its readers retired
-                if (i + 1 < n_ch) {
-                    if (!(ok = wait(&bars.g3, par))) break;
-                    load_c(i + 1);
+                if (!(ok = g4_done && g2_done && c_next)) break;
+                // ---- B(i+1) once G4(i) retired, x(i+1) once G2(i) retired
+                if (more) {
                     if (!(ok = wait(&bars.g4, par))) break;
                     load_b(i + 1);
                     if (!(ok = wait(&bars.g2, par))) break;
@@ -329,27 +373,12 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
         }
         if (!ok && lane == 0 && p.fault) atomicCAS(p.fault, 0u, kFaultMmaOut);
     } else if (role == kR3B) {
-        // ================= W_b: B' = w B, in place ==========================
-        const int r = tid - 32 * 12;
+        // ================= W_b: half of B' = w B, in place ==================
         for (int i = 0; i < n_ch; ++i) {
             if (!(ok = role3_wait(p, &bars.acc1, (uint32_t)(i & 1), role, kFaultMmaOut))) break;
             if (!(ok = role3_wait(p, &bars.v_full[i % k3Ring], (uint32_t)((i / k3Ring) & 1), role, kFaultMmaOut)))
                 break;
-            const float* wv = slot(i) + 256;
-            uint8_t* bh = sm + O3_B;
-#pragma unroll 4
-            for (int k = 0; k < 2048 / k3RoleThreads; ++k) {
-                const int q = r + k3RoleThreads * k;  // atom q >> 10, token row (q >> 3) & 127, chunk q & 7
-                const int j = (q >> 3) & 127;
-                const uint32_t off = (uint32_t)(q >> 10) * 16384u + sw128_off(j, q & 7);
-                const float wj = wv[j];
-                uint4 hi, lo;
-                split_xw8_x3(*reinterpret_cast<const uint4*>(bh + off), *reinterpret_cast<const uint4*>(bh + 32768 + off),
-                             f2_of(wj, wj), hi, lo);
-                *reinterpret_cast<uint4*>(bh + off) = hi;
-                *reinterpret_cast<uint4*>(bh + 32768 + off) = lo;
-            }
-            fence_async_smem();
+            scale_b(sm + O3_B, slot(i) + 256, tid - 32 * 12);
             warp_arrive3(&bars.b_ready);
             warp_arrive3(&bars.v_empty[i % k3Ring]);
         }
@@ -365,13 +394,15 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
             const float* Lc2 = vs + 128;
             const float Lt = Lc2[row];
             const bool split = vs[512] != 0.0f;
+            const int mh = warp >= 16 ? 1 : 0;  // tokens j 64 mh .. 64 mh + 63
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int qq = 0; qq < 2; ++qq) {
+                const int q = 2 * mh + qq;
                 float d[32];
                 tmem_ld16(tm + lane_off + T3_D1 + 32 * q, *reinterpret_cast<float(*)[16]>(d));
                 tmem_ld16(tm + lane_off + T3_D1 + 32 * q + 16, *reinterpret_cast<float(*)[16]>(d + 16));
                 tmem_wait_ld();
-                if (q == 3) {
+                if (qq == 1) {
                     tc_fence_before();
                     warp_arrive3(&bars.d1_read);
                 }
@@ -454,10 +485,14 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
             warp_arrive3(&bars.s_ready);
         }
         for (int i = 0; i < n_ch; ++i) {
-            // G4(i) retired, and G3(i) before it: D4 is ready, S_i's copy free
-            if (!(ok = role3_wait(p, &bars.g4, (uint32_t)(i & 1), role, kFaultMmaOut))) break;
+            // first the other half of B'(i), once G1(i) has read B(i)
+            if (!(ok = role3_wait(p, &bars.acc1, (uint32_t)(i & 1), role, kFaultMmaOut))) break;
             if (!(ok = role3_wait(p, &bars.v_full[i % k3Ring], (uint32_t)((i / k3Ring) & 1), role, kFaultMmaOut)))
                 break;
+            scale_b(sm + O3_B, slot(i) + 256, 128 + (tid - 32 * 8));
+            warp_arrive3(&bars.b_ready);
+            // G4(i) retired, and G3(i) before it: D4 is ready, S_i's copy free
+            if (!(ok = role3_wait(p, &bars.g4, (uint32_t)(i & 1), role, kFaultMmaOut))) break;
             tc_fence_after();
             const float decay = ex2(slot(i)[128 + kCS - 1]);
             const bool more = i + 1 < n_ch;

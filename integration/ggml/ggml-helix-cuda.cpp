@@ -30,12 +30,14 @@
 // per-token kernel (the crossover is measured on B200 by measure_gate.py).
 // ggml applies no clamp to softplus(dt), so neither does the descriptor.
 //
-// Precision.  By default the scan runs on the exact fp32 kernels (ggml's own
-// op test is calibrated at fp32 accuracy, as the reference bridge notes);
-// GGML_HELIX_BF16=1 opts into the tensor-core path (x, B, C rounded to bf16
-// once by a cast kernel, fp32 accumulators and carried state), the
-// counterpart of the reference's GGML_HELIX_MPP=1.  GGML_HELIX_DISABLE=1
-// turns the hook off.
+// Precision.  By default the scan runs on HELIX's fp32-class tensor-core
+// kernels (every fp32 operand as a bf16 hi + lo pair, three products per
+// GEMM, fp32 accumulators and state: about 1e-5 relative L2 against fp64,
+// far inside what ggml's op test accepts for fp32, which is why the
+// reference bridge kept its bf16 path opt-in).  GGML_HELIX_BF16=1 opts into
+// the bf16 tensor-core path (x, B, C rounded to bf16 once), the counterpart
+// of the reference's GGML_HELIX_MPP=1; GGML_HELIX_EXACT=1 selects the exact
+// fp32 CUDA-core kernels; GGML_HELIX_DISABLE=1 turns the hook off.
 //
 // Scratch.  helix never allocates; the bridge keeps one scratch buffer per
 // (thread, device), grown with cudaMalloc outside stream capture.  While the
@@ -68,6 +70,7 @@ constexpr int kDefaultMinTokens = 32;
 struct Settings {
     bool disabled = false;
     bool bf16 = false;
+    bool exact = false;
     int min_tokens = kDefaultMinTokens;
 };
 
@@ -76,6 +79,7 @@ const Settings & settings() {
         Settings r;
         if (const char * e = std::getenv("GGML_HELIX_DISABLE"); e && e[0] == '1') r.disabled = true;
         if (const char * e = std::getenv("GGML_HELIX_BF16"); e && e[0] == '1') r.bf16 = true;
+        if (const char * e = std::getenv("GGML_HELIX_EXACT"); e && e[0] == '1') r.exact = true;
         if (const char * e = std::getenv("GGML_HELIX_MIN_TOKENS")) r.min_tokens = std::atoi(e);
         return r;
     }();
@@ -209,7 +213,7 @@ bool build_desc(const ggml_tensor * op, helix_scan_desc * d) {
     d->multipass = true;
     d->io_dtype = HELIX_F32;
     d->compute_dtype = settings().bf16 ? HELIX_BF16 : HELIX_F32;
-    d->backend = HELIX_BACKEND_AUTO;
+    d->backend = settings().exact ? HELIX_BACKEND_REF : HELIX_BACKEND_AUTO;
     return true;
 }
 
