@@ -5,16 +5,18 @@
 // all three with TMA from bf16 tiles).
 //
 // The copies are dense, in the caller's scratch (Plan::cast regions):
-//   x  -> [S][L][H][Pp]  with Pp = head_dim rounded up to 8 (TMA strides must
-//                        be multiples of 16 bytes); channels P..Pp-1 hold 0
-//   B, C -> [S][L][G][N] (d_state is a multiple of 8)
+//   x  -> [S][L][H][Pp]  bf16 (bf16 family), Pp = head_dim rounded up to 8
+//                        (TMA strides must be multiples of 16 bytes), or fp32
+//                        (three-product family, only when TMA cannot read x
+//                        as stored), Pp = head_dim rounded up to 4; channels
+//                        P..Pp-1 hold 0
+//   B, C -> [S][L][G][N] bf16 (d_state is a multiple of 8)
 // Rounding is to nearest even, the same as the checkers' bf16 widening.
 // For the three-product family (scan_tc3.cu) the kernel also writes the low
-// halves, lo = bf16(v - hi), into copies of the same layout: hi + lo carries
-// v to about 16 significant bits.
+// halves of B and C, lo = bf16(v - hi), into copies of the same layout:
+// hi + lo carries v to about 16 significant bits.
 // HBM-bound: 4 bytes read and 2 (4 with the low halves) written per element,
-// one quad of four consecutive elements per thread step, 16-byte loads where
-// the source rows are contiguous and aligned.
+// 16-byte loads where the source rows are contiguous and aligned.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -29,8 +31,9 @@ namespace {
 constexpr int kCastThreads = 256;
 
 struct CastDst {
-    __nv_bfloat16 *x, *b, *c;
-    __nv_bfloat16 *xl, *bl, *cl;  // low halves (three-product family), else null
+    __nv_bfloat16 *x, *b, *c;     // x: null when x is not copied
+    __nv_bfloat16 *bl, *cl;       // low halves (three-product family), else null
+    float* xf;                    // fp32 copy of x (three-product family), else null
     int pp;  // padded head_dim of the x copy
 };
 
@@ -70,8 +73,18 @@ __device__ __forceinline__ void cast_quad(const float* row, int64_t stride, int 
     put4(dst, dst_lo, v);
 }
 
+// x quad k..k+3 of one row as fp32 (elements past `width` are zero).
+__device__ __forceinline__ void copy_quad(const float* row, int64_t stride, int k, int width, float* dst) {
+    float4 v;
+    v.x = k < width ? __ldg(row + (int64_t)k * stride) : 0.0f;
+    v.y = k + 1 < width ? __ldg(row + (int64_t)(k + 1) * stride) : 0.0f;
+    v.z = k + 2 < width ? __ldg(row + (int64_t)(k + 2) * stride) : 0.0f;
+    v.w = k + 3 < width ? __ldg(row + (int64_t)(k + 3) * stride) : 0.0f;
+    *reinterpret_cast<float4*>(dst) = v;
+}
+
 __global__ void __launch_bounds__(kCastThreads) cast_bf16_kernel(ScanParams p, CastDst d) {
-    const int64_t qx = (int64_t)p.S * p.L * p.H * (d.pp / 4);  // quads of x
+    const int64_t qx = (d.x || d.xf) ? (int64_t)p.S * p.L * p.H * (d.pp / 4) : 0;  // quads of x
     const int64_t qb = (int64_t)p.S * p.L * p.G * (p.N / 4);   // quads of B (and of C)
     const int64_t total = qx + 2 * qb;
     const float* x = static_cast<const float*>(p.x);
@@ -86,7 +99,10 @@ __global__ void __launch_bounds__(kCastThreads) cast_bf16_kernel(ScanParams p, C
             const int64_t st = r / p.H;
             const int t = (int)(st % p.L), seq = (int)(st / p.L);
             const float* row = x + (int64_t)seq * p.seq_x + (int64_t)t * p.s_x0 + (int64_t)h * p.s_x1;
-            cast_quad(row, p.s_x2, k, p.P, d.x + r * d.pp + k, d.xl ? d.xl + r * d.pp + k : nullptr);
+            if (d.xf)
+                copy_quad(row, p.s_x2, k, p.P, d.xf + r * d.pp + k);
+            else
+                cast_quad(row, p.s_x2, k, p.P, d.x + r * d.pp + k, nullptr);
         } else {
             const bool isc = q >= qx + qb;
             const int64_t u = q - qx - (isc ? qb : 0);
@@ -153,23 +169,26 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* stream, bool run) {
     CastDst d;
-    d.x = static_cast<__nv_bfloat16*>(p->cast_x);
+    d.x = pl.x_copy == 1 ? static_cast<__nv_bfloat16*>(p->cast_x) : nullptr;
+    d.xf = pl.x_copy == 2 ? static_cast<float*>(p->cast_x) : nullptr;
     d.b = static_cast<__nv_bfloat16*>(p->cast_b);
     d.c = static_cast<__nv_bfloat16*>(p->cast_c);
-    d.xl = static_cast<__nv_bfloat16*>(p->cast_xl);
     d.bl = static_cast<__nv_bfloat16*>(p->cast_bl);
     d.cl = static_cast<__nv_bfloat16*>(p->cast_cl);
     d.pp = pl.x_pitch;
-    // dense x (copy pitch = head_dim), B and C, all 16-byte aligned: flat copies
-    const bool x_flat = p->s_x2 == 1 && d.pp == p->P && p->s_x1 == p->P && p->s_x0 == (int64_t)p->H * p->P &&
-                        p->seq_x == (int64_t)p->L * p->H * p->P && aligned16(p->x);
+    // dense x (bf16 copy, pitch = head_dim) or no x copy, dense B and C, all
+    // 16-byte aligned: flat copies
+    const bool x_dense = p->s_x2 == 1 && d.pp == p->P && p->s_x1 == p->P && p->s_x0 == (int64_t)p->H * p->P &&
+                         p->seq_x == (int64_t)p->L * p->H * p->P && aligned16(p->x);
+    const bool x_flat = pl.x_copy == 0 || (pl.x_copy == 1 && x_dense);
     const int64_t row_bc = (int64_t)p->G * p->N;
     const bool bc_flat = p->s_b1 == p->N && p->s_b0 == row_bc && p->seq_b == (int64_t)p->L * row_bc &&
                          p->s_c1 == p->N && p->s_c0 == row_bc && p->seq_c == (int64_t)p->L * row_bc &&
                          aligned16(p->B) && aligned16(p->C);
     if (run && x_flat && bc_flat) {
         FlatCast f;
-        f.seg[0] = {static_cast<const float*>(p->x), d.x, d.xl, (int64_t)p->S * p->L * p->H * p->P / 8};
+        f.seg[0] = {static_cast<const float*>(p->x), d.x, nullptr,
+                    pl.x_copy == 1 ? (int64_t)p->S * p->L * p->H * p->P / 8 : 0};
         f.seg[1] = {static_cast<const float*>(p->B), d.b, d.bl, (int64_t)p->S * p->L * row_bc / 8};
         f.seg[2] = {static_cast<const float*>(p->C), d.c, d.cl, (int64_t)p->S * p->L * row_bc / 8};
         const int64_t groups = f.seg[0].n8 + f.seg[1].n8 + f.seg[2].n8;
@@ -180,7 +199,7 @@ int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* strea
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     } else if (run) {
-        const int64_t quads = (int64_t)p->S * p->L * (p->H * (d.pp / 4) + 2 * p->G * (p->N / 4));
+        const int64_t quads = (int64_t)p->S * p->L * ((pl.x_copy ? p->H * (d.pp / 4) : 0) + 2 * p->G * (p->N / 4));
         const int64_t want = (quads + kCastThreads - 1) / kCastThreads;
         const int64_t cap = (int64_t)(ctx ? ctx->n_sm : 148) * 8;  // grid-stride beyond 8 CTAs per SM
         const unsigned grid = (unsigned)(want < cap ? (want > 0 ? want : 1) : cap);
@@ -188,13 +207,15 @@ int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* strea
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    // the kernels that follow read the dense bf16 copies (and the low
-    // halves, with the same strides, from p->cast_xl / cast_bl / cast_cl)
-    p->x = d.x;
-    p->s_x0 = (int64_t)p->H * d.pp;
-    p->s_x1 = d.pp;
-    p->s_x2 = 1;
-    p->seq_x = (int64_t)p->L * p->H * d.pp;
+    // the kernels that follow read the dense copies (and the low halves of B
+    // and C, with the same strides, from p->cast_bl / cast_cl)
+    if (pl.x_copy) {
+        p->x = pl.x_copy == 1 ? static_cast<const void*>(d.x) : static_cast<const void*>(d.xf);
+        p->s_x0 = (int64_t)p->H * d.pp;
+        p->s_x1 = d.pp;
+        p->s_x2 = 1;
+        p->seq_x = (int64_t)p->L * p->H * d.pp;
+    }
     p->B = d.b;
     p->C = d.c;
     p->s_b0 = p->s_c0 = (int64_t)p->G * p->N;

@@ -1551,8 +1551,9 @@ constexpr int kStRing = 4;
 // Shared-memory plan of the state kernel.  bf16: two-deep B and x rings and
 // one xw buffer keep a CTA at 69 KB, so three CTAs share an SM: more CTAs in
 // flight hide the load latency of each step better than deeper rings in
-// fewer CTAs.  Three-product mode (X3): B and x slots hold hi | lo halves,
-// the x ring is one deep, and two CTAs share an SM.
+// fewer CTAs.  Three-product mode (X3): B slots hold hi | lo halves, x slots
+// fp32 x (256-byte rows, read by TMA as stored), the x ring is one deep, and
+// two CTAs share an SM.
 template <bool X3>
 struct StCfg {
     static constexpr int B = 2;                        // B ring depth
@@ -1560,7 +1561,7 @@ struct StCfg {
     static constexpr int Xw = 1;                       // xw buffers
     static constexpr int Ctas = X3 ? 2 : 3;            // CTAs per SM
     static constexpr uint32_t b_slot = X3 ? 32768 : 16384;  // B rows of one step: states 0-63 | 64-127 (| lo)
-    static constexpr uint32_t x_slot = X3 ? 16384 : 8192;   // x rows of one step (| lo)
+    static constexpr uint32_t x_slot = X3 ? 16384 : 8192;   // x rows of one step (bf16, or fp32 with X3)
     static constexpr uint32_t SO_B = 0;
     static constexpr uint32_t SO_X = SO_B + B * b_slot;
     static constexpr uint32_t SO_XW = SO_X + X * x_slot;        // Xw x (hi 8 KB | lo 8 KB)
@@ -1589,8 +1590,8 @@ __device__ __forceinline__ bool st_wait(uint64_t* bar, uint32_t parity, unsigned
 }
 
 //
-// X3 (three-product family): B and x come as bf16 hi | lo pairs; xw is
-// w (x_hi + x_lo) split again, and each K step adds B_lo . xw_hi (N = 64)
+// X3 (three-product family): B comes as bf16 hi | lo pairs and x as fp32;
+// xw is w x split into hi | lo, and each K step adds B_lo . xw_hi (N = 64)
 // into the hi columns, so the state is B_hi xw_hi + B_hi xw_lo + B_lo xw_hi.
 template <bool X3>
 __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
@@ -1674,9 +1675,8 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
     };
     auto load_x = [&](int s) {
         uint64_t* bar = &bars.x_full[s % kStX];
-        mbar_expect_tx(bar, (X3 ? 2 : 1) * 8192);
+        mbar_expect_tx(bar, Cfg::x_slot);
         tma_load_4d(sX(s), &maps.x, bar, p0, tl.h, ts_of(s), tl.seq);
-        if constexpr (X3) tma_load_4d(sX(s) + 8192, &maps.xl, bar, p0, tl.h, ts_of(s), tl.seq);
     };
 
     bool ok = true;
@@ -1684,10 +1684,7 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
         if ((tid & 31) == 0) {
             prefetch_tmap(&maps.b);
             prefetch_tmap(&maps.x);
-            if constexpr (X3) {
-                prefetch_tmap(&maps.bl);
-                prefetch_tmap(&maps.xl);
-            }
+            if constexpr (X3) prefetch_tmap(&maps.bl);
             for (int s = 0; s < kStB && s < n_st; ++s) load_b(s);
             for (int s = 0; s < kStX && s < n_st; ++s) load_x(s);
             for (int s = 0; s < n_st && ok; ++s) {
@@ -1818,11 +1815,12 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
                 const uint32_t off = sw128_off(j, c);
                 const float wj = wv[j];
                 uint4 hi, lo;
-                if constexpr (X3)
-                    split_xw8_x3(*reinterpret_cast<const uint4*>(x + off), *reinterpret_cast<const uint4*>(x + 8192 + off),
-                                 f2_of(wj, wj), hi, lo);
-                else
+                if constexpr (X3) {
+                    const float4* xf = reinterpret_cast<const float4*>(x + j * 256 + c * 32);
+                    split_xw8_f32(xf[0], xf[1], f2_of(wj, wj), hi, lo);
+                } else {
                     split_xw8(*reinterpret_cast<const uint4*>(x + off), f2_of(wj, wj), hi, lo);
+                }
                 *reinterpret_cast<uint4*>(xh + off) = hi;
                 *reinterpret_cast<uint4*>(xh + 8192 + off) = lo;
             }
@@ -1885,16 +1883,13 @@ bool make_y_map(EncodeFn fn, CUtensorMap* m, const ScanParams& p) {
 }
 
 // Maps of the state kernel: x and B in 64-token boxes (its step); with x3,
-// also their low halves (same strides as the bf16 copies p points at).
+// x is fp32 and B has its low half too (same strides as the copy p points at).
 bool make_state_maps(EncodeFn fn, TcMaps* m, const ScanParams& p, bool x3) {
     const int64_t S = p.S;
     std::memset(m, 0, sizeof(*m));
-    if (!make_map(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf) ||
-        !make_map(fn, &m->b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf))
-        return false;
-    if (!x3) return true;
-    return p.cast_xl && p.cast_bl &&
-           make_map(fn, &m->xl, p.cast_xl, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf) &&
+    if (!make_map(fn, &m->b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf)) return false;
+    if (!x3) return make_map(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf);
+    return p.cast_bl && make_map_f32(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf) &&
            make_map(fn, &m->bl, p.cast_bl, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf);
 }
 

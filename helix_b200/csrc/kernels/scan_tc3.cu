@@ -12,9 +12,10 @@
 // artificial intelligence datatype for higher-precision computations",
 // ARITH 2019).  The dropped terms are of order 2^-16 of the product, so the
 // scan lands near 1e-5 relative L2 against the fp64 oracle, an order below
-// the 1e-4 bar of the fp32 path, at tensor-core speed.  x, B and C reach the
-// kernels as hi and lo copies made by the cast kernel (scan_cast.cu); the
-// mask, the carried state and the G4 operand are split on chip.
+// the 1e-4 bar of the fp32 path, at tensor-core speed.  B and C reach the
+// kernels as hi and lo copies made by the cast kernel (scan_cast.cu); x is
+// read as stored, fp32, by TMA and split on chip, like the mask, the carried
+// state and the G4 operand.
 //
 // Same run/span decomposition as the bf16 family (runtime/internal.h): the
 // state kernel (scan_tc.cu, tc_state_kernel<true>) reduces the runs before
@@ -38,22 +39,25 @@
 //   0-3    W_y   y = D2 + e^Lc D3 -> global (one token row per thread)
 //   4-7    W_m   M from D1 -> TMEM, tokens j 0-63 of each row (one row per thread)
 //   16-19  W_m   the same, tokens j 64-127
-//   8-11   W_c   half of B' = w B (in place, re-split into hi | lo), then
-//                S_next in TMEM (fp32) and its hi | lo copy in smem for G3
-//   12-15  W_b   the other half of B'
-//   20     TMA producer and MMA issuer (lane 0)
+//   8-11   W_c   S_next in TMEM (fp32) and its hi | lo copy in smem for G3;
+//                then x(i+1): fp32 through a 64-token staging buffer (its
+//                own TMA loads) into the x hi | lo tiles
+//   12-15  W_b   half of B' = w B (in place, re-split into hi | lo)
+//   0-3    W_y   also the other half of B', before its y
+//   20     TMA producer (C, B) and MMA issuer (lane 0)
 //   21     chunk vectors (dt, Lc, w, split decays) into a 3-slot ring
 // (two warps of every role but W_y's share each SM sub-partition with warps
 // of other roles, so a role's work on the critical path is spread over all
 // four issue units).
 //
 // MMA issue order per chunk: G1, G3, then G4 and G2 in whichever order their
-// operands (B', M) are ready; then C(i+1) once G3 retired, B(i+1) once G4
-// retired, x(i+1) once G2 retired (one buffer each).
+// operands (B', M) are ready; C(i+1) loads once G3 retired, B(i+1) once G4
+// retired, and x(i+1) is converted once G4 and G2 retired (one buffer each).
 //
 // TMEM columns: D1 0-127 | M hi 128-191 | M lo 192-255 | D2 256-319 |
 //               D3 320-383 | D4 384-447 | S 448-511.
-// smem: C hi|lo 64 KB | B hi|lo 64 KB | x hi|lo 32 KB | S hi|lo 32 KB | ring.
+// smem: C hi|lo 64 KB | B hi|lo 64 KB | x hi|lo 32 KB | S hi|lo 32 KB |
+//       x staging 16 KB | ring.
 //
 // Every wait is bounded; an expired wait records a fault code in the device
 // word (helix_device_fault), the CTA lets issued MMAs land, frees its TMEM
@@ -88,7 +92,8 @@ constexpr uint32_t O3_C = 0;          // C hi (two 64-state atoms) | C lo
 constexpr uint32_t O3_B = 65536;      // B hi | B lo (B' after the scaling)
 constexpr uint32_t O3_X = 131072;     // x hi | x lo
 constexpr uint32_t O3_S = 163840;     // S hi | S lo ([n][p])
-constexpr uint32_t O3_V = 196608;     // chunk-vector ring
+constexpr uint32_t O3_XS = 196608;    // fp32 x staging, 64 tokens x 64 channels
+constexpr uint32_t O3_V = 212992;     // chunk-vector ring
 constexpr uint32_t SMEM_3 = O3_V + k3Ring * k3Vec * 4 + 1024;
 static_assert(SMEM_3 <= 232448, "fits one CTA per SM");
 
@@ -100,7 +105,9 @@ constexpr uint32_t ID3_MM = idesc_bf16(128, 64, true, true);     // G4
 constexpr float kSplitSpan2 = 20.0f * kLog2e;                    // in-group span of the split mask
 
 struct Bars3 {
-    uint64_t c_full, b_full, x_full;   // TMA arrivals, one phase per chunk
+    uint64_t c_full, b_full;           // TMA arrivals, one phase per chunk
+    uint64_t xs_full;                  // TMA arrivals, one phase per 64-token half of x
+    uint64_t x_full;                   // W_c: x hi | lo tiles written
     uint64_t acc1, g3, g4, g2;         // MMA commits: G1, G3, G4, G2 of a chunk retired
     uint64_t d1_read, m_ready;         // W_m: D1 read, M written
     uint64_t b_ready;                  // W_b: B' written
@@ -187,7 +194,8 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
     if (tid == 0) {
         mbar_init(&bars.c_full, 1);
         mbar_init(&bars.b_full, 1);
-        mbar_init(&bars.x_full, 1);
+        mbar_init(&bars.xs_full, 1);
+        mbar_init(&bars.x_full, 4);
         mbar_init(&bars.acc1, 1);
         mbar_init(&bars.g3, 1);
         mbar_init(&bars.g4, 1);
@@ -234,22 +242,13 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
                 tma_load_4d(sm + O3_B + 32768, &maps.bl, &bars.b_full, nb, g, t0, tl.seq);
                 tma_load_4d(sm + O3_B + 49152, &maps.bl, &bars.b_full, nb + 64, g, t0, tl.seq);
             };
-            auto load_x = [&](int i) {
-                const int t0 = t_begin + i * kCS;
-                mbar_expect_tx(&bars.x_full, 2 * 16384);
-                tma_load_4d(sm + O3_X, &maps.x, &bars.x_full, p0, tl.h, t0, tl.seq);
-                tma_load_4d(sm + O3_X + 16384, &maps.xl, &bars.x_full, p0, tl.h, t0, tl.seq);
-            };
             prefetch_tmap(&maps.c);
             prefetch_tmap(&maps.cl);
             prefetch_tmap(&maps.b);
             prefetch_tmap(&maps.bl);
-            prefetch_tmap(&maps.x);
-            prefetch_tmap(&maps.xl);
             if (n_ch > 0) {
                 load_c(0);
                 load_b(0);
-                load_x(0);
             }
             const uint32_t aC = smem_u32(sm + O3_C), aB = smem_u32(sm + O3_B);
             const uint32_t aX = smem_u32(sm + O3_X), aS = smem_u32(sm + O3_S);
@@ -321,12 +320,10 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
                     if (clock64() - t_start > kWaitBudget) break;
                 }
                 if (!(ok = g4_done && g2_done && c_next)) break;
-                // ---- B(i+1) once G4(i) retired, x(i+1) once G2(i) retired
+                // ---- B(i+1) once G4(i) retired
                 if (more) {
                     if (!(ok = wait(&bars.g4, par))) break;
                     load_b(i + 1);
-                    if (!(ok = wait(&bars.g2, par))) break;
-                    load_x(i + 1);
                 }
             }
             if (!ok) {
@@ -456,6 +453,50 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
             *reinterpret_cast<uint4*>(sS + sw128_off(row, q)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
             *reinterpret_cast<uint4*>(sS + 16384 + sw128_off(row, q)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
         };
+        // x: fp32 halves of 64 tokens through the staging buffer; the role's
+        // first thread issues each load once the whole role has read the
+        // previous one out
+        const bool xs_leader = tid == 32 * 8;
+        uint32_t xs_phase = 0;
+        auto xs_load = [&](int chunk, int half) {
+            mbar_expect_tx(&bars.xs_full, 16384);
+            tma_load_4d(sm + O3_XS, &maps.x, &bars.xs_full, p0, tl.h, t_begin + chunk * kCS + 64 * half, tl.seq);
+        };
+        // x(chunk) as bf16 hi | lo tiles (MN-major, token rows), then x_full
+        auto convert_x = [&](int chunk) -> bool {
+            const int r = tid - 32 * 8;
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half) {
+                if (!role3_wait(p, &bars.xs_full, xs_phase & 1u, role, kFaultTmaOut)) return false;
+                ++xs_phase;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int q = r + 128 * k;  // token row q >> 3 of the half, channel chunk q & 7
+                    const int j = q >> 3, c = q & 7;
+                    const float4* src = reinterpret_cast<const float4*>(sm + O3_XS + j * 256 + c * 32);
+                    uint4 hi, lo;
+                    split8_f32(src[0], src[1], hi, lo);
+                    const uint32_t off = sw128_off(64 * half + j, c);
+                    *reinterpret_cast<uint4*>(sm + O3_X + off) = hi;
+                    *reinterpret_cast<uint4*>(sm + O3_X + 16384 + off) = lo;
+                }
+                named_sync(1 + role, 128);  // the staging buffer is read out
+                if (xs_leader) {
+                    fence_async_smem();
+                    if (half == 0)
+                        xs_load(chunk, 1);
+                    else if (chunk + 1 < n_ch)
+                        xs_load(chunk + 1, 0);  // lands while this chunk is computed
+                }
+            }
+            fence_async_smem();
+            warp_arrive3(&bars.x_full);
+            return true;
+        };
+        if (xs_leader) {
+            prefetch_tmap(&maps.x);
+            if (n_ch > 0) xs_load(0, 0);
+        }
         {
             grid_dep_wait();  // the carry kernel's span-entry states
             const float* src;
@@ -484,15 +525,12 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
             fence_async_smem();
             warp_arrive3(&bars.s_ready);
         }
-        for (int i = 0; i < n_ch; ++i) {
-            // first the other half of B'(i), once G1(i) has read B(i)
-            if (!(ok = role3_wait(p, &bars.acc1, (uint32_t)(i & 1), role, kFaultMmaOut))) break;
-            if (!(ok = role3_wait(p, &bars.v_full[i % k3Ring], (uint32_t)((i / k3Ring) & 1), role, kFaultMmaOut)))
-                break;
-            scale_b(sm + O3_B, slot(i) + 256, 128 + (tid - 32 * 8));
-            warp_arrive3(&bars.b_ready);
+        if (n_ch > 0) ok = convert_x(0);
+        for (int i = 0; i < n_ch && ok; ++i) {
             // G4(i) retired, and G3(i) before it: D4 is ready, S_i's copy free
             if (!(ok = role3_wait(p, &bars.g4, (uint32_t)(i & 1), role, kFaultMmaOut))) break;
+            if (!(ok = role3_wait(p, &bars.v_full[i % k3Ring], (uint32_t)((i / k3Ring) & 1), role, kFaultMmaOut)))
+                break;
             tc_fence_after();
             const float decay = ex2(slot(i)[128 + kCS - 1]);
             const bool more = i + 1 < n_ch;
@@ -515,6 +553,11 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
                 warp_arrive3(&bars.s_ready);
             }
             warp_arrive3(&bars.v_empty[i % k3Ring]);
+            // x(i+1) over x(i) once G2(i) retired too (G4(i) already has)
+            if (more) {
+                if (!(ok = role3_wait(p, &bars.g2, (uint32_t)(i & 1), role, kFaultMmaOut))) break;
+                if (!(ok = convert_x(i + 1))) break;
+            }
         }
         if (ok && last && n < p.N) {
             float* s1 = p.s1 + (int64_t)tl.seq * p.seq_s + (int64_t)tl.h * p.s_s0 + (int64_t)p0 * p.s_s1 + n;
@@ -533,10 +576,14 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
         // ================= W_y ==============================================
         grid_dep_wait();  // y of the previous 128-state pass, when adding to it
         for (int i = 0; i < n_ch; ++i) {
-            // G2(i) retired, and G3(i) before it
-            if (!(ok = role3_wait(p, &bars.g2, (uint32_t)(i & 1), role, kFaultMmaOut))) break;
+            // first the other half of B'(i), once G1(i) has read B(i)
+            if (!(ok = role3_wait(p, &bars.acc1, (uint32_t)(i & 1), role, kFaultMmaOut))) break;
             if (!(ok = role3_wait(p, &bars.v_full[i % k3Ring], (uint32_t)((i / k3Ring) & 1), role, kFaultMmaOut)))
                 break;
+            scale_b(sm + O3_B, slot(i) + 256, 128 + tid);
+            warp_arrive3(&bars.b_ready);
+            // G2(i) retired, and G3(i) before it
+            if (!(ok = role3_wait(p, &bars.g2, (uint32_t)(i & 1), role, kFaultMmaOut))) break;
             tc_fence_after();
             const int tp = t_begin + i * kCS;
             const int tlen = t_end - tp;
@@ -590,13 +637,13 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
     }
 }
 
-// Maps of the output kernel: x, B, C and their low halves in 128-token boxes.
+// Maps of the output kernel: fp32 x in 64-token boxes (the staging halves),
+// B and C and their low halves in 128-token boxes.
 bool make_tc3_maps(EncodeFn fn, TcMaps* m, const ScanParams& p) {
     const int64_t S = p.S;
     std::memset(m, 0, sizeof(*m));
-    if (!p.cast_xl || !p.cast_bl || !p.cast_cl) return false;
-    return make_map(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x) &&
-           make_map(fn, &m->xl, p.cast_xl, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x) &&
+    if (!p.cast_bl || !p.cast_cl) return false;
+    return make_map_f32(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, 64) &&
            make_map(fn, &m->b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b) &&
            make_map(fn, &m->bl, p.cast_bl, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b) &&
            make_map(fn, &m->c, p.C, p.N, p.G, p.L, S, p.s_c1, p.s_c0, p.seq_c) &&

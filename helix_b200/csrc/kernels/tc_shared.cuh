@@ -110,5 +110,18 @@ inline bool make_map(EncodeFn fn, CUtensorMap* m, const void* base, int64_t inne
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 4-D fp32 map (inner, d1, tok, seq) with a 64 x 1 x box_tok x 1 box and no
+// swizzle (256-byte rows): fp32 x read in place by the three-product family.
+inline bool make_map_f32(EncodeFn fn, CUtensorMap* m, const void* base, int64_t inner, int64_t d1, int64_t tok,
+                         int64_t seq, int64_t s1, int64_t s_tok, int64_t s_seq, int box_tok) {
+    cuuint64_t dims[4] = {(cuuint64_t)inner, (cuuint64_t)d1, (cuuint64_t)tok, (cuuint64_t)seq};
+    cuuint64_t strides[3] = {(cuuint64_t)(s1 * 4), (cuuint64_t)(s_tok * 4), (cuuint64_t)(s_seq * 4)};
+    cuuint32_t box[4] = {64, 1, (cuuint32_t)box_tok, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace tc
 }  // namespace hx

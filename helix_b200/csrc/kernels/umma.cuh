@@ -358,5 +358,41 @@ __device__ __forceinline__ void split_xw8_x3(const uint4& xh, const uint4& xl, u
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// Eight fp32 values (a, b) times w, as bf16 hi = round(v w) and
+// lo = round(v w - hi).
+__device__ __forceinline__ void split_xw8_f32(const float4& a, const float4& b, uint64_t w2, uint4& hi, uint4& lo) {
+    const uint64_t in[4] = {f2_of(a.x, a.y), f2_of(a.z, a.w), f2_of(b.x, b.y), f2_of(b.z, b.w)};
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const uint64_t p = f2_mul(in[e], w2);
+        float p0, p1;
+        f2_to(p, p0, p1);
+        h[e] = pack_bf16x2(p0, p1);
+        float l0, l1;
+        f2_to(f2_sub(p, f2_of_bf16x2(h[e])), l0, l1);
+        l[e] = pack_bf16x2(l0, l1);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Eight fp32 values as bf16 hi = round(v) and lo = round(v - hi).
+__device__ __forceinline__ void split8_f32(const float4& a, const float4& b, uint4& hi, uint4& lo) {
+    const uint64_t in[4] = {f2_of(a.x, a.y), f2_of(a.z, a.w), f2_of(b.x, b.y), f2_of(b.z, b.w)};
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        float v0, v1;
+        f2_to(in[e], v0, v1);
+        h[e] = pack_bf16x2(v0, v1);
+        float l0, l1;
+        f2_to(f2_sub(in[e], f2_of_bf16x2(h[e])), l0, l1);
+        l[e] = pack_bf16x2(l0, l1);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 }  // namespace umma
 }  // namespace hx

@@ -192,21 +192,33 @@ void lay_out_scratch(const helix_scan_desc& d, Plan* pl) {
     add_cast_regions(d, pl);
 }
 
-// The bf16 copies of F32-stored x, B, C at the end of the scratch (and their
-// low halves for the three-product family).
+// Whether TMA can read x as stored (fp32, innermost stride 1, the other
+// strides multiples of 16 bytes): the three-product family then reads it in
+// place.  The base address is checked when the call binds its tensors.
+bool x_tma_f32(const helix_scan_desc& d) {
+    return d.s_x[2] == 1 && d.s_x[0] > 0 && d.s_x[1] > 0 && d.seq_x > 0 && (d.s_x[0] * 4) % 16 == 0 &&
+           (d.s_x[1] * 4) % 16 == 0 && (d.seq_x * 4) % 16 == 0;
+}
+
+// The copies of F32-stored inputs at the end of the scratch: bf16 x, B, C for
+// the bf16 family; bf16 hi and lo halves of B and C (and, only where TMA cannot
+// read x as stored, a dense fp32 copy of x) for the three-product family.
 void add_cast_regions(const helix_scan_desc& d, Plan* pl) {
     if (!pl->cast) return;
-    pl->x_pitch = (d.head_dim + 7) / 8 * 8;
+    const bool x3 = pl->path == kPathTcX3;
+    pl->x_copy = x3 ? (x_tma_f32(d) ? 0 : 2) : 1;
+    pl->x_pitch = pl->x_copy == 2 ? (d.head_dim + 3) / 4 * 4 : (d.head_dim + 7) / 8 * 8;
     const size_t rows = (size_t)d.n_seq * d.n_tok;
+    const size_t x_bytes = pl->x_copy == 0 ? 0 : rows * d.n_head * pl->x_pitch * (pl->x_copy == 2 ? 4 : 2);
+    const size_t bc_bytes = rows * d.n_group * d.d_state * 2;
     pl->off_xc = pl->total;
-    pl->off_bc = pl->off_xc + align256(rows * d.n_head * pl->x_pitch * 2);
-    pl->off_cc = pl->off_bc + align256(rows * d.n_group * d.d_state * 2);
-    pl->total = pl->off_cc + align256(rows * d.n_group * d.d_state * 2);
+    pl->off_bc = pl->off_xc + align256(x_bytes);
+    pl->off_cc = pl->off_bc + align256(bc_bytes);
+    pl->total = pl->off_cc + align256(bc_bytes);
     if (!pl->cast_lo) return;
-    pl->off_xl = pl->total;
-    pl->off_bl = pl->off_xl + align256(rows * d.n_head * pl->x_pitch * 2);
-    pl->off_cl = pl->off_bl + align256(rows * d.n_group * d.d_state * 2);
-    pl->total = pl->off_cl + align256(rows * d.n_group * d.d_state * 2);
+    pl->off_bl = pl->total;
+    pl->off_cl = pl->off_bl + align256(bc_bytes);
+    pl->total = pl->off_cl + align256(bc_bytes);
 }
 
 }  // namespace

@@ -146,6 +146,11 @@ helix_status bind_call(helix_ctx* ctx, const helix_scan_desc& d, const Plan& pl,
             return HELIX_ERR_UNSUPPORTED_SHAPE;
         }
     }
+    if (pl.path == kPathTcX3 && pl.x_copy == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) != 0) {
+        // TMA reads x in place
+        set_error(ctx, "x must be 16-byte aligned for the tensor-core fp32 path");
+        return HELIX_ERR_UNSUPPORTED_SHAPE;
+    }
     return HELIX_OK;
 }
 
@@ -160,7 +165,6 @@ void bind_scratch(const Plan& pl, char* base, ScanParams* p) {
         p->cast_c = base + pl.off_cc;
     }
     if (pl.cast_lo) {
-        p->cast_xl = base + pl.off_xl;
         p->cast_bl = base + pl.off_bl;
         p->cast_cl = base + pl.off_cl;
     }
@@ -217,6 +221,7 @@ void fill_params(ScanParams& p, const helix_scan_desc& d, const Plan& pl) {
     p.s_s0 = d.s_s[0]; p.s_s1 = d.s_s[1]; p.seq_s = d.seq_s;
     p.s_y0 = d.s_y[0]; p.s_y1 = d.s_y[1]; p.s_y2 = d.s_y[2]; p.seq_y = d.seq_y;
     p.s_a = d.s_a;
+    p.x_copy = pl.x_copy;
     const int64_t row = (int64_t)(d.n_head - 1) * d.s_s[0] + (int64_t)(d.head_dim - 1) * d.s_s[1] + d.d_state;
     p.s_row_bytes = row * (int64_t)sizeof(float);
     p.s1_bytes = ((int64_t)(d.n_seq - 1) * d.seq_s + row) * (int64_t)sizeof(float);

@@ -73,13 +73,16 @@ struct Plan {
     // Tensor-core family with x, B, C stored F32: dense bf16 copies made by a
     // cast kernel first (multipass only; single pass takes the fp32 family).
     bool   cast     = false;
-    int    x_pitch  = 0;    // channels per row of the x copy (head_dim rounded up to 8)
-    size_t off_xc   = 0;    // bf16 [seq][tok][head][x_pitch]
+    // x: 1 = bf16 copy (bf16 family); for the three-product family, which
+    // reads fp32 x by TMA and splits it on chip, 0 = none (x read in place)
+    // or 2 = dense fp32 copy (x strides TMA cannot describe).
+    int    x_copy   = 0;
+    int    x_pitch  = 0;    // channels per row of the x copy (bf16: head_dim rounded up to 8; fp32: to 4)
+    size_t off_xc   = 0;    // [seq][tok][head][x_pitch]
     size_t off_bc   = 0;    // bf16 [seq][tok][group][d_state]
     size_t off_cc   = 0;    // bf16 [seq][tok][group][d_state]
-    // Three-product family: the low halves of the copies, same layouts.
+    // Three-product family: the low halves of the B and C copies, same layouts.
     bool   cast_lo  = false;
-    size_t off_xl   = 0;
     size_t off_bl   = 0;
     size_t off_cl   = 0;
     size_t total    = 0;    // scratch bytes
@@ -131,9 +134,9 @@ struct ScanParams {
     void*          cast_x;      // scratch: bf16 copies (Plan::cast), else null
     void*          cast_b;
     void*          cast_c;
-    void*          cast_xl;     // scratch: their low halves (Plan::cast_lo), else null
-    void*          cast_bl;
+    void*          cast_bl;     // scratch: low halves of the B and C copies (Plan::cast_lo), else null
     void*          cast_cl;
+    int32_t        x_copy;      // Plan::x_copy
 
     unsigned*      fault;       // the device fault word (helix_device_fault)
     int64_t        s_row_bytes; // bytes one s0 / s1 row spans
@@ -205,13 +208,13 @@ int launch_simt_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p
 int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 int launch_tc3_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 // kernels/scan_tc.cu, shared with scan_tc3.cu: the tcgen05 state kernel over
-// `runs` runs (x3: the three-product mode, reading the low halves from
-// p.cast_xl / p.cast_bl), and the carry kernel (programmatic dependent of
-// the previous kernel when after_ours).
+// `runs` runs (x3: the three-product mode, reading fp32 x and the low halves
+// of B from p.cast_bl), and the carry kernel (programmatic dependent of the
+// previous kernel when after_ours).
 int launch_tc_state_pass(const helix_ctx* ctx, const ScanParams& p, int runs, bool x3, void* stream);
 int launch_tc_carry(const ScanParams& p, bool after_ours, void* stream);
-// kernels/scan_cast.cu: when `run`, enqueues the bf16 copies of x, B, C into
-// p->cast_*; then points *p at the copies (dense strides, io_bf16 = 1).
+// kernels/scan_cast.cu: when `run`, enqueues the copies of x (Plan::x_copy),
+// B and C into p->cast_*; then points *p at the copies (dense strides).
 int launch_cast(const helix_ctx* ctx, const Plan& pl, ScanParams* p, void* stream, bool run);
 // kernels/scan_shard.cu
 // state[seq][h] = fold over runs of (exp(lam_r) S + agg_r) from zero, written

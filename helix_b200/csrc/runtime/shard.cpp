@@ -92,6 +92,10 @@ extern "C" helix_status helix_scan_shard_state(helix_ctx* ctx, void* stream, con
             return HELIX_ERR_UNSUPPORTED_SHAPE;
         }
     }
+    if (pl.path == hx::kPathTcX3 && pl.x_copy == 0 && (reinterpret_cast<uintptr_t>(p.x) & 15) != 0) {
+        hx::set_error(ctx, "x must be 16-byte aligned for the tensor-core fp32 path");
+        return HELIX_ERR_UNSUPPORTED_SHAPE;
+    }
     DeviceScope ds(ctx->device);
     int rc = pl.path == hx::kPathTcBf16 ? hx::launch_tc_states(ctx, pl, p, stream)
              : pl.path == hx::kPathTcX3 ? hx::launch_tc3_states(ctx, pl, p, stream)
