@@ -9,6 +9,7 @@
 //   tc_state_kernel        the state each run leaves from a zero start (G4 over
 //                          the run) and its log-decay
 //   tc_carry_kernel        run states -> the states entering each output span
+//   tc_carry_seg_kernel    the same for more than eight runs, folded in segments
 //   tc_out_kernel          the output pass, fast path: two 64-channel slabs of
 //                          one group per CTA, transposed GEMMs (see below)
 //   tc_out_general_kernel  the output pass for the tiles the fast path leaves
@@ -1473,11 +1474,109 @@ __global__ void __launch_bounds__(kOutThreads, 1)
 // the run states from a zero start into span-entry states, in place:
 //   S = s0[ids[seq]];  for r < state_runs:  S = exp(lam_r) S + agg_r;
 //   agg_r <- S  where run r + 1 starts an output span ((r + 1) % out_k == 0)
-// so afterwards slot k*out_k - 1 holds the state entering span k.  One thread
-// per float4 of one (seq, head)'s [P][N] state; the loads of successive runs
-// are independent, so several are kept in flight.
+// so afterwards slot k*out_k - 1 holds the state entering span k.
+//
+// The fold is associative ((a1, b1) then (a2, b2) = (a1 a2, a2 b1 + b2)), so
+// with more than kCarrySeg runs (tc_carry_seg_kernel) the runs are cut into
+// segments of up to kCarrySeg runs: a thread holds one
+// float4 of one (seq, head)'s [P][N] state for one segment, loads all of its
+// segment's run states at once (one round trip however many runs there are),
+// folds them from zero, and posts the segment's fold to shared memory; each
+// thread then takes its entry state from s0 and the folds of the segments
+// before it, and walks its segment again from registers, storing the span-
+// entry states.  A CTA holds kCarryThreads / n_seg_p2 float4s of one head
+// for every segment.  Up to kCarrySeg runs, tc_carry_kernel walks them in
+// order, one thread per float4 with four loads in flight: it needs half the
+// registers, so more CTAs stay resident.
 // ---------------------------------------------------------------------------
 constexpr int kCarryThreads = 256;
+constexpr int kCarrySeg = 8;  // runs per segment
+
+__host__ __device__ constexpr int carry_segs_p2(int runs) {
+    int n = (runs + kCarrySeg - 1) / kCarrySeg, q = 1;
+    while (q < n) q <<= 1;
+    return q;  // <= 32 for up to kMaxRuns runs
+}
+
+__global__ void __launch_bounds__(kCarryThreads) tc_carry_seg_kernel(ScanParams p) {
+    grid_dep_wait();    // the state kernel's run states
+    grid_dep_launch();  // the output kernel may start its prologue
+    __shared__ float4 seg_b[kCarryThreads];  // [element][segment] fold of each segment from zero
+    __shared__ float seg_a[32];              // per segment: sum of its log-decays
+    const int R = p.state_runs, K = p.out_k;
+    const int nseg = (R + kCarrySeg - 1) / kCarrySeg;
+    const int sp2 = carry_segs_p2(R);
+    const int per_cta = kCarryThreads / sp2;        // float4 elements per CTA
+    const int64_t per_head4 = (int64_t)p.P * p.N / 4;
+    const int64_t blocks_per_head = (per_head4 + per_cta - 1) / per_cta;
+    const int64_t head_lin = (int64_t)blockIdx.x / blocks_per_head;  // seq * H + h
+    if (head_lin >= (int64_t)p.S * p.H) return;
+    const int seg = (int)threadIdx.x % sp2;
+    const int el = (int)threadIdx.x / sp2;
+    const int64_t e4 = ((int64_t)blockIdx.x % blocks_per_head) * per_cta + el;
+    const bool live = e4 < per_head4 && seg < nseg;
+    const int seq = (int)(head_lin / p.H), h = (int)(head_lin % p.H);
+    const int64_t unit0 = head_lin * p.run_slots;
+    float4* agg = reinterpret_cast<float4*>(p.agg + unit0 * (int64_t)p.P * p.N) + e4;
+    const int r0 = seg * kCarrySeg, r1 = min(R, r0 + kCarrySeg);
+
+    // this segment's run states and decays, all loads in flight at once
+    float4 v[kCarrySeg];
+    float lamv[kCarrySeg];
+    float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lsum = 0.f;
+    if (live) {
+#pragma unroll
+        for (int k = 0; k < kCarrySeg; ++k) {
+            if (r0 + k < r1) {
+                v[k] = agg[(int64_t)(r0 + k) * per_head4];
+                lamv[k] = p.lam[unit0 + r0 + k];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kCarrySeg; ++k) {
+            if (r0 + k < r1) {
+                const float a = expf(lamv[k]);
+                b.x = fmaf(a, b.x, v[k].x);
+                b.y = fmaf(a, b.y, v[k].y);
+                b.z = fmaf(a, b.z, v[k].z);
+                b.w = fmaf(a, b.w, v[k].w);
+                lsum += lamv[k];
+            }
+        }
+    }
+    seg_b[threadIdx.x] = b;
+    if (el == 0 && seg < 32) seg_a[seg] = lsum;
+    __syncthreads();
+    if (!live) return;
+    // entry state of this segment: s0, then the folds of the segments before it
+    const int c = (int)((4 * e4) / p.N), n = (int)((4 * e4) % p.N);  // N % 4 == 0
+    int src;
+    const bool clear = s0_row(p, seq, &src);
+    const float* s0 = p.s0 + (int64_t)src * p.seq_s + (int64_t)h * p.s_s0 + (int64_t)c * p.s_s1 + n;
+    float4 S = clear ? make_float4(s0[0], s0[1], s0[2], s0[3]) : make_float4(kNaN, kNaN, kNaN, kNaN);
+    for (int k = 0; k < seg; ++k) {
+        const float a = expf(seg_a[k]);
+        const float4 bk = seg_b[el * sp2 + k];
+        S.x = fmaf(a, S.x, bk.x);
+        S.y = fmaf(a, S.y, bk.y);
+        S.z = fmaf(a, S.z, bk.z);
+        S.w = fmaf(a, S.w, bk.w);
+    }
+    // the segment again, from registers: span-entry states where a span starts
+#pragma unroll
+    for (int k = 0; k < kCarrySeg; ++k) {
+        const int r = r0 + k;
+        if (r < r1) {
+            const float a = expf(lamv[k]);
+            S.x = fmaf(a, S.x, v[k].x);
+            S.y = fmaf(a, S.y, v[k].y);
+            S.z = fmaf(a, S.z, v[k].z);
+            S.w = fmaf(a, S.w, v[k].w);
+            if ((r + 1) % K == 0) agg[(int64_t)r * per_head4] = S;
+        }
+    }
+}
 
 __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
     grid_dep_wait();    // the state kernel's run states
@@ -1525,6 +1624,16 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
     }
 }
 
+// CTAs of the carry kernel: per (seq, head), enough for its float4 elements
+// at kCarryThreads / (segments, rounded up to a power of two) per CTA.
+unsigned carry_grid(const ScanParams& p) {
+    const int64_t per_head4 = (int64_t)p.P * p.N / 4;
+    if (p.state_runs <= kCarrySeg)
+        return (unsigned)(((int64_t)p.S * p.H * per_head4 + kCarryThreads - 1) / kCarryThreads);
+    const int per_cta = kCarryThreads / carry_segs_p2(p.state_runs);
+    return (unsigned)((int64_t)p.S * p.H * ((per_head4 + per_cta - 1) / per_cta));
+}
+
 // ---------------------------------------------------------------------------
 // State kernel: the run's state from a zero start, G4 accumulated over the
 // whole run in one TMEM accumulator, plus the run's log-decay.  Sized for
@@ -1546,26 +1655,29 @@ __global__ void __launch_bounds__(kCarryThreads) tc_carry_kernel(ScanParams p) {
 // ---------------------------------------------------------------------------
 constexpr int kStEpi = 256;
 constexpr int kStThreads = kStEpi + 64;
-constexpr int kStHalf = 64;                            // tokens per step
 constexpr int kStRing = 4;
-// Shared-memory plan of the state kernel.  bf16: two-deep B and x rings and
-// one xw buffer keep a CTA at 69 KB, so three CTAs share an SM: more CTAs in
-// flight hide the load latency of each step better than deeper rings in
-// fewer CTAs.  Three-product mode (X3): B slots hold hi | lo halves, x slots
-// fp32 x (256-byte rows, read by TMA as stored), the x ring is one deep, and
-// two CTAs share an SM.
+// Shared-memory plan of the state kernel: two-deep B and x rings and one xw
+// buffer, so three CTAs share an SM: more CTAs in flight hide the load
+// latency of each step better than deeper rings in fewer CTAs.  bf16 mode:
+// 64-token steps, 69 KB.  Three-product mode (X3): 32-token steps (B slots
+// hold hi | lo halves, x slots fp32 x in 256-byte rows read by TMA as
+// stored), 61 KB.
 template <bool X3>
 struct StCfg {
+    static constexpr int T = X3 ? 32 : 64;             // tokens per step
+    static constexpr int SPC = 128 / T;                // steps per 128-token chunk
     static constexpr int B = 2;                        // B ring depth
-    static constexpr int X = X3 ? 1 : 2;               // x ring depth
+    static constexpr int X = 2;                        // x ring depth
     static constexpr int Xw = 1;                       // xw buffers
-    static constexpr int Ctas = X3 ? 2 : 3;            // CTAs per SM
-    static constexpr uint32_t b_slot = X3 ? 32768 : 16384;  // B rows of one step: states 0-63 | 64-127 (| lo)
-    static constexpr uint32_t x_slot = X3 ? 16384 : 8192;   // x rows of one step (bf16, or fp32 with X3)
+    static constexpr int Ctas = 3;                     // CTAs per SM
+    static constexpr uint32_t atom = T * 128;          // one 64-element-wide SW128 tile of T rows
+    static constexpr uint32_t b_slot = (X3 ? 4 : 2) * atom;  // B: states 0-63 | 64-127 (| lo halves)
+    static constexpr uint32_t x_slot = X3 ? T * 256 : atom;  // x rows of one step (bf16, or fp32 with X3)
+    static constexpr uint32_t xw_slot = 2 * atom;             // xw hi | lo
     static constexpr uint32_t SO_B = 0;
     static constexpr uint32_t SO_X = SO_B + B * b_slot;
-    static constexpr uint32_t SO_XW = SO_X + X * x_slot;        // Xw x (hi 8 KB | lo 8 KB)
-    static constexpr uint32_t SO_W = SO_XW + Xw * 16384;        // kStRing x 128 weights
+    static constexpr uint32_t SO_XW = SO_X + X * x_slot;
+    static constexpr uint32_t SO_W = SO_XW + Xw * xw_slot;      // kStRing x 128 weights
     static constexpr uint32_t SO_DT = SO_W + kStRing * 512;     // vector warp's raw dt ring, 4 x 128 floats
     static constexpr uint32_t SMEM = SO_DT + 4 * 512 + 1024;
 };
@@ -1597,7 +1709,8 @@ template <bool X3>
 __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
     tc_state_kernel(const __grid_constant__ TcMaps maps, ScanParams p, int runs_in_grid) {
     using Cfg = StCfg<X3>;
-    constexpr int kStB = Cfg::B, kStX = Cfg::X, kStXw = Cfg::Xw;
+    constexpr int kStB = Cfg::B, kStX = Cfg::X, kStXw = Cfg::Xw, kT = Cfg::T, kSpc = Cfg::SPC;
+    constexpr uint32_t kAtom = Cfg::atom;
     constexpr uint32_t SO_B = Cfg::SO_B, SO_X = Cfg::SO_X, SO_XW = Cfg::SO_XW, SO_W = Cfg::SO_W, SO_DT = Cfg::SO_DT;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
@@ -1623,10 +1736,10 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
     const int t_begin = tl.run * p.run_tok;
     const int t_end = min(p.L, t_begin + p.run_tok);
     const int n_ch = (t_end - t_begin + kCS - 1) / kCS;
-    const int n_st = 2 * n_ch;  // steps; a step past t_end reads zeros
+    const int n_st = kSpc * n_ch;  // steps; a step past t_end reads zeros
     const int64_t db = (int64_t)tl.seq * p.seq_dt + (int64_t)tl.h * p.s_dt1;
     auto t0_of = [&](int q) { return t_begin + (n_ch - 1 - q) * kCS; };       // visit order q -> chunk
-    auto ts_of = [&](int s) { return t0_of(s >> 1) + (s & 1) * kStHalf; };    // step s -> first token
+    auto ts_of = [&](int s) { return t0_of(s / kSpc) + (s % kSpc) * kT; };    // step s -> first token
     // the decay-weight warp issues the dt loads of its first three chunks
     // before any set-up, so their latency overlaps it and the first TMA waits
     float r0[4], r1[4], r2[4];
@@ -1637,7 +1750,7 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
     }
     auto sB = [&](int s) { return sm + SO_B + (uint32_t)(s % kStB) * Cfg::b_slot; };
     auto sX = [&](int s) { return sm + SO_X + (uint32_t)(s % kStX) * Cfg::x_slot; };
-    auto sXW = [&](int s) { return sm + SO_XW + (uint32_t)(s % kStXw) * 16384u; };
+    auto sXW = [&](int s) { return sm + SO_XW + (uint32_t)(s % kStXw) * Cfg::xw_slot; };
 
     if (tid == 0) {
         for (int k = 0; k < kStB; ++k) {
@@ -1665,12 +1778,12 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
 
     auto load_b = [&](int s) {
         uint64_t* bar = &bars.b_full[s % kStB];
-        mbar_expect_tx(bar, (X3 ? 4 : 2) * 8192);
+        mbar_expect_tx(bar, Cfg::b_slot);
         tma_load_4d(sB(s), &maps.b, bar, nb, g, ts_of(s), tl.seq);
-        tma_load_4d(sB(s) + 8192, &maps.b, bar, nb + 64, g, ts_of(s), tl.seq);
+        tma_load_4d(sB(s) + kAtom, &maps.b, bar, nb + 64, g, ts_of(s), tl.seq);
         if constexpr (X3) {
-            tma_load_4d(sB(s) + 16384, &maps.bl, bar, nb, g, ts_of(s), tl.seq);
-            tma_load_4d(sB(s) + 24576, &maps.bl, bar, nb + 64, g, ts_of(s), tl.seq);
+            tma_load_4d(sB(s) + 2 * kAtom, &maps.bl, bar, nb, g, ts_of(s), tl.seq);
+            tma_load_4d(sB(s) + 3 * kAtom, &maps.bl, bar, nb + 64, g, ts_of(s), tl.seq);
         }
     };
     auto load_x = [&](int s) {
@@ -1693,17 +1806,17 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
                 if (!(ok = mbar_wait(&bars.xw_full[s % kStXw], (uint32_t)((s / kStXw) & 1), kWaitBudget))) break;
                 tc_fence_after();
                 // A = B rows of the step (M = 128 states in two 64-state atoms),
-                // B = [xw_hi | xw_lo] (N = 128 in two atoms), K = 64 tokens
-                const uint64_t dA = sdesc_sw128(smem_u32(sB(s)), 8192, 1024);
-                const uint64_t dX = sdesc_sw128(smem_u32(sXW(s)), 8192, 1024);
+                // B = [xw_hi | xw_lo] (N = 128 in two atoms), K = the step's tokens
+                const uint64_t dA = sdesc_sw128(smem_u32(sB(s)), kAtom, 1024);
+                const uint64_t dX = sdesc_sw128(smem_u32(sXW(s)), kAtom, 1024);
 #pragma unroll
-                for (int ks = 0; ks < 4; ++ks)
+                for (int ks = 0; ks < kT / 16; ++ks)
                     mma_bf16(tm, desc_add(dA, 2048u * ks), desc_add(dX, 2048u * ks), ID_G4W, (s > 0 || ks > 0) ? 1u : 0u);
                 if constexpr (X3) {
                     // B_lo . xw_hi into the hi columns
-                    const uint64_t dAl = sdesc_sw128(smem_u32(sB(s)) + 16384u, 8192, 1024);
+                    const uint64_t dAl = sdesc_sw128(smem_u32(sB(s)) + 2 * kAtom, kAtom, 1024);
 #pragma unroll
-                    for (int ks = 0; ks < 4; ++ks)
+                    for (int ks = 0; ks < kT / 16; ++ks)
                         mma_bf16(tm, desc_add(dAl, 2048u * ks), desc_add(dX, 2048u * ks), ID_G4W64, 1u);
                 }
                 mma_commit(&bars.xw_empty[s % kStXw]);
@@ -1796,8 +1909,8 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
     } else {
         // ---- xw builders: two 16-byte x vectors per thread per step -------
         for (int s = 0; s < n_st; ++s) {
-            const int q = s >> 1, slot = q % kStRing;
-            if ((s & 1) == 0) {
+            const int q = s / kSpc, sub = s % kSpc, slot = q % kStRing;
+            if (sub == 0) {
                 if (!(ok = st_wait(&bars.w_full[slot], (uint32_t)((q / kStRing) & 1), kFaultMmaState))) break;
             }
             if (!(ok = st_wait(&bars.x_full[s % kStX], (uint32_t)((s / kStX) & 1), kFaultTmaState))) break;
@@ -1805,11 +1918,11 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
                 if (!(ok = st_wait(&bars.xw_empty[s % kStXw], (uint32_t)(((s - kStXw) / kStXw) & 1), kFaultMmaState)))
                     break;
             }
-            const float* wv = wring + slot * 128 + (s & 1) * kStHalf;
+            const float* wv = wring + slot * 128 + sub * kT;
             const uint8_t* x = sX(s);
             uint8_t* xh = sXW(s);
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {
+            for (int k = 0; k < kT * 8 / kStEpi; ++k) {
                 const int i = tid + kStEpi * k;
                 const int j = i >> 3, c = i & 7;
                 const uint32_t off = sw128_off(j, c);
@@ -1822,13 +1935,13 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
                     split_xw8(*reinterpret_cast<const uint4*>(x + off), f2_of(wj, wj), hi, lo);
                 }
                 *reinterpret_cast<uint4*>(xh + off) = hi;
-                *reinterpret_cast<uint4*>(xh + 8192 + off) = lo;
+                *reinterpret_cast<uint4*>(xh + kAtom + off) = lo;
             }
             fence_async_smem();
             __syncwarp();
             if ((tid & 31) == 0) {
                 mbar_arrive(&bars.xw_full[s % kStXw]);
-                if (s & 1) mbar_arrive(&bars.w_empty[slot]);
+                if (sub == kSpc - 1) mbar_arrive(&bars.w_empty[slot]);
             }
         }
         // all G4 MMAs retired: the last step's commit
@@ -1886,11 +1999,12 @@ bool make_y_map(EncodeFn fn, CUtensorMap* m, const ScanParams& p) {
 // x is fp32 and B has its low half too (same strides as the copy p points at).
 bool make_state_maps(EncodeFn fn, TcMaps* m, const ScanParams& p, bool x3) {
     const int64_t S = p.S;
+    const int T = x3 ? StCfg<true>::T : StCfg<false>::T;
     std::memset(m, 0, sizeof(*m));
-    if (!make_map(fn, &m->b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf)) return false;
-    if (!x3) return make_map(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf);
-    return p.cast_bl && make_map_f32(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, kStHalf) &&
-           make_map(fn, &m->bl, p.cast_bl, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, kStHalf);
+    if (!make_map(fn, &m->b, p.B, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, T)) return false;
+    if (!x3) return make_map(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, T);
+    return p.cast_bl && make_map_f32(fn, &m->x, p.x, p.P, p.H, p.L, S, p.s_x1, p.s_x0, p.seq_x, T) &&
+           make_map(fn, &m->bl, p.cast_bl, p.N, p.G, p.L, S, p.s_b1, p.s_b0, p.seq_b, T);
 }
 
 // Test hook: HELIX_TC_GENERAL=1 sends every CTA of the output kernel down
@@ -1928,9 +2042,8 @@ int launch_tc_state_pass(const helix_ctx* ctx, const ScanParams& p, int runs, bo
 }
 
 int launch_tc_carry(const ScanParams& p, bool after_ours, void* stream) {
-    const int64_t n4 = (int64_t)p.S * p.H * p.P * p.N / 4;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((n4 + kCarryThreads - 1) / kCarryThreads));
+    cfg.gridDim = dim3(carry_grid(p));
     cfg.blockDim = dim3(kCarryThreads);
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];
@@ -1938,7 +2051,8 @@ int launch_tc_carry(const ScanParams& p, bool after_ours, void* stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = after_ours ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, tc_carry_kernel, p);
+    return p.state_runs <= kCarrySeg ? cudaLaunchKernelEx(&cfg, tc_carry_kernel, p)
+                                     : cudaLaunchKernelEx(&cfg, tc_carry_seg_kernel, p);
 }
 
 int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void* stream) {
@@ -1988,9 +2102,9 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void
     const bool state_ran = pl.need_state_kernel && do_a;
     const bool carry_ran = pl.need_state_kernel && do_b;
     if (carry_ran) {
-        const int64_t n4 = (int64_t)S * p.H * p.P * p.N / 4;
-        const cudaError_t e = launch(tc_carry_kernel, (unsigned)((n4 + kCarryThreads - 1) / kCarryThreads),
-                                     kCarryThreads, 0, state_ran, p);
+        const cudaError_t e = p.state_runs <= kCarrySeg
+                                  ? launch(tc_carry_kernel, carry_grid(p), kCarryThreads, 0, state_ran, p)
+                                  : launch(tc_carry_seg_kernel, carry_grid(p), kCarryThreads, 0, state_ran, p);
         if (e != cudaSuccess) return e;
     }
     if (do_c) {

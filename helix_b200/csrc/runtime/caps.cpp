@@ -130,7 +130,7 @@ namespace {
 // cut into runs fine enough that the state kernel (state_ctas CTAs per SM)
 // has enough CTAs to spread over.
 void tc_split(const helix_scan_desc& d, int blocks, int n_sm, int max_runs, int slabs_per_cta, int state_ctas,
-              int* run_blocks, int* out_k) {
+              int steps_per_block, int* run_blocks, int* out_k) {
     const int64_t units = (int64_t)(d.n_head / d.n_group) * ((d.head_dim + kSlab - 1) / kSlab);
     const int64_t pairs = (int64_t)d.n_seq * d.n_group * ((units + slabs_per_cta - 1) / slabs_per_cta);
     double best = 1e300;
@@ -150,7 +150,7 @@ void tc_split(const helix_scan_desc& d, int blocks, int n_sm, int max_runs, int 
     if (n_out > 1) {
         // Runs per span for the state kernel: each CTA reduces one run of one
         // slab, state_ctas CTAs share an SM, and a CTA costs about
-        // kStateStartSteps 64-token steps of set-up on top of two steps per
+        // kStateStartSteps steps of set-up on top of steps_per_block steps per
         // 128-token block.  Pick the divisor of the span that minimises
         // waves x per-CTA steps, within the run-slot budget.
         const int64_t st_units = (int64_t)d.n_seq * d.n_head * ((d.head_dim + kSlab - 1) / kSlab) * (n_out - 1);
@@ -160,7 +160,7 @@ void tc_split(const helix_scan_desc& d, int blocks, int n_sm, int max_runs, int 
             if (sb % c != 0) continue;
             if ((int64_t)(blocks + sb / c - 1) / (sb / c) > max_runs) break;
             const int64_t waves = (st_units * c + slots - 1) / slots;
-            const double cost = (double)waves * (kStateStartSteps + 2.0 * (sb / c));
+            const double cost = (double)waves * (kStateStartSteps + (double)steps_per_block * (sb / c));
             if (cost < kbest) {
                 kbest = cost;
                 k = c;
@@ -240,9 +240,9 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
         if (const int f = forced_run_tokens()) {
             run_blocks = std::max(1, f / kRunQuantum);
         } else if (pl.path == kPathTcBf16) {
-            tc_split(d, blocks, n_sm, max_runs, 2, kStateCtasPerSm, &run_blocks, &out_k);
+            tc_split(d, blocks, n_sm, max_runs, 2, kStateCtasPerSm, 2, &run_blocks, &out_k);
         } else if (pl.path == kPathTcX3) {
-            tc_split(d, blocks, n_sm, max_runs, 1, kStateCtasPerSmX3, &run_blocks, &out_k);
+            tc_split(d, blocks, n_sm, max_runs, 1, kStateCtasPerSmX3, 4, &run_blocks, &out_k);
         } else {
             // Enough CTAs in the output kernel to cover every SM a few times.
             const int64_t units = (int64_t)d.n_seq * d.n_head * pl.n_pslab;

@@ -37,7 +37,7 @@ constexpr int kMaxRuns = 256;
 // Tensor-core state kernel: CTAs resident per SM, and its fixed cost per CTA
 // (first loads, first decay weights, drain) in 64-token steps, as measured.
 constexpr int kStateCtasPerSm = 3;
-constexpr int kStateCtasPerSmX3 = 2;  // three-product family (larger rings)
+constexpr int kStateCtasPerSmX3 = 3;  // three-product family (32-token steps)
 constexpr double kStateStartSteps = 3.5;
 
 enum Path : int {

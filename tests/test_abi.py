@@ -89,3 +89,36 @@ def test_tensor_core_scratch_plan_c3():
     flags = al(8 * 4 * 4 * 4)
     spans = al(64 * 8 * 4)
     assert lib.helix_scan_scratch_size(None, C.byref(d)) == agg + lam + flags + spans
+
+
+def test_fp32_tensor_core_scratch_plan_c2():
+    """BASELINE config 2 (F32-stored x, B, C; compute F32: the three-product
+    tensor-core family) on a 148-SM part: one 64-channel slab per output CTA,
+    two output spans of 8 chunks (128 CTAs), the first span cut into 4 runs of
+    256 tokens for the state kernel; scratch = 4 run states and log-decays per
+    head, then bf16 hi and lo copies of B and C.  x is read in place (dense
+    fp32), so there is no x copy; a view of x TMA cannot describe (channels two
+    floats apart) adds a dense fp32 copy."""
+    lib = abi.load()
+
+    def desc():
+        d = abi.desc_init(2048, 1, 64, 64, 128, 8)
+        d.io_dtype = 0  # HELIX_F32
+        d.compute_dtype = 0
+        d.multipass = True
+        return d
+
+    def al(n):
+        return (n + 255) // 256 * 256
+
+    agg = al(64 * 4 * 64 * 128 * 4)
+    lam = al(64 * 4 * 4)
+    bc = al(2048 * 8 * 128 * 2)
+    d = desc()
+    assert lib.helix_scan_scratch_size(None, C.byref(d)) == agg + lam + 4 * bc
+    d = desc()
+    d.s_x[2] = 2  # channels two floats apart
+    d.s_x[1] = 2 * 64
+    d.s_x[0] = 64 * 2 * 64
+    d.seq_x = 2048 * 64 * 2 * 64
+    assert lib.helix_scan_scratch_size(None, C.byref(d)) == agg + lam + al(2048 * 64 * 64 * 4) + 4 * bc

@@ -261,3 +261,27 @@ def test_golden_bf16(ctx, oracle, run_tokens, path):
             c = compare(got, want, BF16_REL, BF16_ABS)
             record(f"golden bf16 {path.stem} {name} runs={rt}", ratio=c["ratio"], rl2=c["rel_l2"])
             assert c["ok"] and c["rel_l2"] <= BF16_RL2, (path.stem, name, rt, c)
+
+
+@pytest.mark.parametrize("compute", ["bf16", "f32"])
+def test_carry_over_many_runs(ctx, oracle, run_tokens, compute):
+    """A run boundary every 128 tokens of 8192: 63 runs carried by the carry
+    kernel, folded in segments of eight that combine through shared memory
+    (the span-entry state of every 128-token span), on both tensor-core
+    families."""
+    shape = (8192, 1, 2, 64, 128, 1)
+    prob = oracle.harness_problem(*shape, 31337, True)
+    prob["s0"] = np.random.default_rng(8).normal(0, 0.2, prob["s0"].shape).astype(np.float32)
+    io = "bf16" if compute == "bf16" else "f32"
+    w = widen(prob, io)
+    y_ref, s_ref = _oracle(oracle, w, shape)
+    run_tokens("128")
+    y, s1, d = run(ctx, prob, multipass=True, io=io, compute=compute)
+    assert ctx.plan_info(d).state_runs == 63
+    if compute == "bf16":
+        check_bf16("bf16 63 carried runs", y, s1, y_ref, s_ref)
+    else:
+        from gpu_harness import X3_ABS, X3_REL, X3_RL2
+        for got, want in ((y, y_ref), (s1, s_ref)):
+            c = compare(got, want, X3_REL, X3_ABS)
+            assert c["ok"] and c["rel_l2"] <= X3_RL2, c
