@@ -919,9 +919,9 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
         __syncwarp();
     } else if (warp == kPWarpVec) {
         // ================= chunk vectors of both slabs =======================
-        // Slot 0 was filled by the kernel prologue.  Raw dt of chunk i+3 is
-        // loaded while chunk i is processed and parked in a private
-        // shared-memory ring (no register rotation to wait on).
+        // Slot 0 and the raw dt of chunks 1..3 come from the kernel prologue.
+        // Raw dt of chunk i+3 is loaded while chunk i is processed and parked
+        // in a private shared-memory ring (no register rotation to wait on).
         float* dtr = reinterpret_cast<float*>(sm + OP_DT);  // [4][2][128]
         const float A2[2] = {pt.s[0].Ah * kLog2e, pt.s[1].Ah * kLog2e};
         auto park = [&](int c, const float (&r0)[4], const float (&r1)[4]) {
@@ -933,16 +933,7 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             }
         };
         if (lane == 0 && n_ch > 0) mbar_arrive(&bars.v_full[0]);
-        {
-            float r[3][2][4];
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                warp_load_dt(p, pt.s[0].db, t_begin + (c + 1) * kCS, t_end, r[c][0]);
-                warp_load_dt(p, pt.s[1].db, t_begin + (c + 1) * kCS, t_end, r[c][1]);
-            }
-#pragma unroll
-            for (int c = 0; c < 3; ++c) park(c + 1, r[c][0], r[c][1]);
-        }
+        // raw dt of chunks 1..3 was parked by the kernel prologue
         __syncwarp();
 #pragma unroll 1
         for (int i = 1; i < n_ch && ok; ++i) {
@@ -1358,13 +1349,27 @@ __global__ void __launch_bounds__(kPThreads, 1)
         load_state_tile(p, pt, st, tid);
         if (!p.run_span) pair_span(p, pt, warp, kPEpi + kPBld, &span_bits);
     } else if (warp == kPWarpVec) {
-        // the chunk vectors of chunk 0 straight into ring slot 0
+        // raw dt of chunks 0..3 (token-major loads, far apart: several us
+        // under load), issued before anything waits; chunk 0's vectors
+        // straight into ring slot 0, chunks 1..3 parked in the dt ring
         float* vs = reinterpret_cast<float*>(sm + OP_V);
+        float* dtr = reinterpret_cast<float*>(sm + OP_DT);  // [4][2][128]
         const int tlen = min(kCS, pt.t_end - pt.t_begin);
+        float r[4][2][4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int v = 0; v < 2; ++v) warp_load_dt(p, pt.s[v].db, pt.t_begin + c * kCS, pt.t_end, r[c][v]);
+#pragma unroll
+        for (int c = 1; c < 4; ++c)
+#pragma unroll
+            for (int v = 0; v < 2; ++v)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) dtr[(c & 3) * 256 + 128 * v + 4 * lane + k] = r[c][v][k];
 #pragma unroll
         for (int v = 0; v < 2; ++v) {
-            float raw[4], dv[4], lc[4], total;
-            warp_load_dt(p, pt.s[v].db, pt.t_begin, pt.t_end, raw);
+            float dv[4], lc[4], total;
+            const float (&raw)[4] = r[0][v];
             warp_chunk_prefix(p, 0, pt.t_begin, tlen, pt.s[v].Ah * kLog2e, raw, dv, lc, &total);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {

@@ -94,7 +94,8 @@ constexpr uint32_t O3_X = 131072;     // x hi | x lo
 constexpr uint32_t O3_S = 163840;     // S hi | S lo ([n][p])
 constexpr uint32_t O3_XS = 196608;    // fp32 x staging, 64 tokens x 64 channels
 constexpr uint32_t O3_V = 212992;     // chunk-vector ring
-constexpr uint32_t SMEM_3 = O3_V + k3Ring * k3Vec * 4 + 1024;
+constexpr uint32_t O3_DT = O3_V + k3Ring * k3Vec * 4;  // vector warp's raw dt ring, 4 x 128 floats
+constexpr uint32_t SMEM_3 = O3_DT + 4 * 512 + 1024;
 static_assert(SMEM_3 <= 232448, "fits one CTA per SM");
 
 constexpr uint32_t T3_D1 = 0, T3_MH = 128, T3_ML = 192, T3_D2 = 256, T3_D3 = 320, T3_D4 = 384, T3_S = 448;
@@ -336,12 +337,30 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
         __syncwarp();
     } else if (warp == k3WarpVec) {
         // ================= chunk vectors ====================================
+        // raw dt (token-major loads, far apart: several us under load) runs
+        // three chunks ahead through a private shared-memory ring; the first
+        // three chunks' loads go out together
         const float Ah2 = Ah * kLog2e;
-        float raw[4], raw_next[4];
-        if (n_ch > 0) warp_load_dt(p, db, t_begin, t_end, raw);
+        float* dtr = reinterpret_cast<float*>(sm + O3_DT);
+        auto park = [&](int c, const float (&r)[4]) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dtr[(c & 3) * 128 + 4 * lane + k] = r[k];
+        };
+        {
+            float r[3][4];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) warp_load_dt(p, db, t_begin + min(c, max(n_ch - 1, 0)) * kCS, t_end, r[c]);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) park(c, r[c]);
+        }
+        __syncwarp();
         for (int i = 0; i < n_ch && ok; ++i) {
             const int t0 = t_begin + i * kCS;
-            if (i + 1 < n_ch) warp_load_dt(p, db, t0 + kCS, t_end, raw_next);
+            float nx[4];
+            const bool more = i + 3 < n_ch;
+            if (more) warp_load_dt(p, db, t0 + 3 * kCS, t_end, nx);
+            const float raw[4] = {dtr[(i & 3) * 128 + 4 * lane], dtr[(i & 3) * 128 + 4 * lane + 1],
+                                  dtr[(i & 3) * 128 + 4 * lane + 2], dtr[(i & 3) * 128 + 4 * lane + 3]};
             float v[4], pre[4], total;
             warp_chunk_prefix(p, db, t0, min(kCS, t_end - t0), Ah2, raw, v, pre, &total);
             if (i >= k3Ring) {
@@ -365,8 +384,8 @@ __global__ void __launch_bounds__(k3Threads, 1) tc3_out_kernel(const __grid_cons
             if (lane == 0) vs[512] = all_ok ? 1.0f : 0.0f;
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars.v_full[i % k3Ring]);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) raw[k] = raw_next[k];
+            if (more) park(i + 3, nx);
+            __syncwarp();
         }
         if (!ok && lane == 0 && p.fault) atomicCAS(p.fault, 0u, kFaultMmaOut);
     } else if (role == kR3B) {
