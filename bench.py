@@ -5,8 +5,8 @@ bf16, dt/A/s0 f32, y/s1 f32, multipass.  Under torchrun the 64 heads of that
 one problem are split over the ranks in whole head groups (8 heads per rank
 at N=8); heads never interact, so there is no collective on the data path
 ("scaling": "strong").  `value` = the problem's tokens over the max device
-time of any rank.  --scaling weak gives every rank its own 64-head block
-instead (value counts tokens x heads / 64, summed over ranks).
+time of any rank.  --scaling weak gives every rank its own copy of the problem
+instead (value counts every rank's tokens).
 
 Timing: W warm-up steps, then K steps; before each step a 256 MiB buffer is
 written (flushing the 126 MB L2; the flush is outside the timed events); each
@@ -510,9 +510,9 @@ def main():
     tj = ROOT / "profiles" / "ncu_traffic.json"
     if tj.exists() and not strong:
         traffic = json.loads(tj.read_text()).get(f"{a.config}/{a.compute}", {}).get("dram_bytes_per_launch")
-    # tokens of the problem the job processed: the whole head set once
-    # (strong), or one 64-head block per rank (weak)
-    job_tok = gshape.S * gshape.L * (1.0 if strong else world * shape.H / 64.0)
+    # tokens the job processed: the problem's tokens (one GPU, or its heads
+    # split over the ranks), or every rank's own copy of the problem (weak)
+    job_tok = gshape.S * gshape.L * (world if a.scaling == "weak" and world > 1 else 1)
     path_gbs = shape.alg_bytes() / (ms_per_step * 1e-3) / 1e9
     tflops = (gshape.flops() if strong else world * shape.flops()) / (ms_per_step * 1e-3) / 1e12
 
@@ -599,7 +599,7 @@ def main():
         layout = (f"the problem's {gshape.H} heads split over {world} ranks in whole groups "
                   f"({shape.H} heads per rank)")
     elif world > 1:
-        layout = "per rank its own 64-head block of a head-sharded layer"
+        layout = "per rank its own copy of the problem (weak scaling)"
     else:
         layout = "one GPU"
     line = {
