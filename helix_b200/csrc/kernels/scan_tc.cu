@@ -644,8 +644,8 @@ __device__ __forceinline__ void out_general(const TcMaps& maps, const ScanParams
 //
 // TMEM columns: D1 0-127 | Y 128-255 | D4 256-383 | S~ (bf16 pairs) 384-447.
 // smem: C/B 2 x 64 KB | xw hi 32 KB | xw lo 32 KB (slab tiles 16 KB apart) |
-//       vector ring | raw dt ring.  The span-entry state is staged over the
-//       xw buffers before the first chunk.
+//       vector ring | raw dt ring.  The span-entry state is staged in chunk
+//       1's C/B stage before the first chunk (chunk 1's C/B follows it there).
 // ---------------------------------------------------------------------------
 constexpr uint32_t OP_XW = 131072;
 constexpr uint32_t OP_V = 196608;
@@ -848,7 +848,7 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             mbar_init(&bars.v_full[k], 1);
             mbar_init(&bars.v_empty[k], kPBld + kPEpi);
         }
-        cb_issued = n_ch < 2 ? n_ch : 2;  // chunks 0 and 1: the kernel prologue
+        cb_issued = n_ch < 1 ? n_ch : 1;  // chunk 0: the kernel prologue
         cb_landed = 0;
         fence_mbar_init();
     }
@@ -882,6 +882,11 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
                 const uint64_t dC = sdesc_sw128(aC, 16, 1024);              // C, then the mask (K-major)
                 const uint64_t dBm = sdesc_sw128(aC + 32768, 16384, 1024);  // B as MN-major
                 if (!(ok = mbar_wait(&bars.s_ready, par, kWaitBudget))) break;
+                if (i == 0 && n_ch > 1) {
+                    // the epilogue has moved the span-entry state out of stage 1
+                    load_cb_chunk(maps, sm + OO_CB + 65536u, &cb_bar[1], pt.g, t_begin + kCS, pt.seq, p.n_base);
+                    cb_issued = 2;
+                }
                 if (i >= 1 && !(ok = mbar_wait(&bars.y_free, (uint32_t)((i - 1) & 1), kWaitBudget))) break;
                 tc_fence_after();
 #pragma unroll
@@ -980,9 +985,8 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             // out, by when it has landed
             if (i + 1 < n_ch) load_x_pair(p, pt, xl, i + 1, nxt);
             if (!(ok = warp_wait(&bars.v_full[i % kPRing], vpar(i)))) break;
-            // lo(i-1) was read by G4(i-1) only; before chunk 0, the epilogue
-            // reads the span-entry state staged over these buffers
-            if (!(ok = i >= 1 ? warp_wait(&bars.g4, (uint32_t)((i - 1) & 1)) : warp_wait(&bars.s_ready, 0u))) break;
+            // lo(i-1) was read by G4(i-1) only
+            if (i >= 1 && !(ok = warp_wait(&bars.g4, (uint32_t)((i - 1) & 1)))) break;
             // rows of this thread's vectors: j0 + 12 k; the swizzled 16-byte
             // column depends on the row only through bit 2 (k odd flips it)
             const float* wv = slot(i) + kPSlot * xl.sl + xl.j0;
@@ -1073,9 +1077,9 @@ __device__ __forceinline__ void out_pair(const TcMaps& maps, const ScanParams& p
             }
         };
         if (n_ch > 0 && (ok = warp_wait(&bars.v_full[0], 0u))) {
-            // the span-entry state, staged by the kernel prologue over the xw
-            // buffers (the builders wait for s_ready before their first store)
-            const float* st = reinterpret_cast<const float*>(sm + OP_XW);
+            // the span-entry state, staged by the kernel prologue in chunk 1's
+            // C/B stage (the MMA thread loads chunk 1 there after s_ready)
+            const float* st = reinterpret_cast<const float*>(sm + OO_CB + 65536u);
             const float e0 = slot(0)[kPSlot * v + 256];
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2) {
@@ -1333,12 +1337,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
         prefetch_tmap(&maps.x);
         prefetch_tmap(&maps.b);
         prefetch_tmap(&maps.c);
-        for (int i = 0; i < 2 && i < pt.n_ch; ++i)
-            load_cb_chunk(maps, sm + OO_CB + (uint32_t)i * 65536u, &cb_bar[i], pt.g, pt.t_begin + i * kCS, pt.seq,
-                          p.n_base);
+        if (pt.n_ch > 0) load_cb_chunk(maps, sm + OO_CB, &cb_bar[0], pt.g, pt.t_begin, pt.seq, p.n_base);
     }
     float pre[4 * kPV];  // x of chunk 0 (builders)
-    float* st = reinterpret_cast<float*>(sm + OP_XW);  // free until the builders start
+    // the span-entry state is staged in chunk 1's C/B stage, which takes
+    // chunk 1's C/B once the epilogue has moved the state into TMEM; the xw
+    // buffers stay free for the builders' first chunk
+    float* st = reinterpret_cast<float*>(sm + OO_CB + 65536u);
     if (warp < kPEpi) {
         // launched behind the carry kernel, this kernel may run its prologue
         // early: everything above reads only the scan's inputs; the carry
@@ -1396,8 +1401,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     if (tid == 0 && p.tile_flag) p.tile_flag[blockIdx.x] = fast ? 1 : 0;
     if (!fast) {
         // the general kernel does this tile: let the C/B loads land first
-        if (tid == kPMmaTid)
-            for (int i = 0; i < 2 && i < pt.n_ch; ++i) mbar_wait(&cb_bar[i], 0u, kWaitBudget);
+        if (tid == kPMmaTid && pt.n_ch > 0) mbar_wait(&cb_bar[0], 0u, kWaitBudget);
         __syncthreads();
         if (warp == kPWarpMma) tmem_dealloc(tm, 512);
         return;
