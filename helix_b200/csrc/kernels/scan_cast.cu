@@ -83,7 +83,12 @@ __device__ __forceinline__ void copy_quad(const float* row, int64_t stride, int 
     *reinterpret_cast<float4*>(dst) = v;
 }
 
+// The state kernel, launched behind this one as a programmatic dependent,
+// may start at once: it waits (griddepcontrol.wait) before reading a copy.
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __global__ void __launch_bounds__(kCastThreads) cast_bf16_kernel(ScanParams p, CastDst d) {
+    allow_dependents();
     const int64_t qx = (d.x || d.xf) ? (int64_t)p.S * p.L * p.H * (d.pp / 4) : 0;  // quads of x
     const int64_t qb = (int64_t)p.S * p.L * p.G * (p.N / 4);   // quads of B (and of C)
     const int64_t total = qx + 2 * qb;
@@ -146,6 +151,7 @@ __device__ __forceinline__ void cast8(const FlatSeg& g, int64_t k) {
 }
 
 __global__ void __launch_bounds__(kCastThreads) cast_flat_kernel(FlatCast f) {
+    allow_dependents();
     const int64_t n0 = f.seg[0].n8, n1 = n0 + f.seg[1].n8, total = n1 + f.seg[2].n8;
     const int64_t stride = (int64_t)gridDim.x * kCastThreads;
     for (int64_t q = (int64_t)blockIdx.x * kCastThreads + threadIdx.x; q < total; q += 2 * stride) {

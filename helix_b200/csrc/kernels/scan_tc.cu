@@ -1807,8 +1807,17 @@ __global__ void __launch_bounds__(kStThreads, StCfg<X3>::Ctas)
             prefetch_tmap(&maps.b);
             prefetch_tmap(&maps.x);
             if constexpr (X3) prefetch_tmap(&maps.bl);
+            // Launched behind the cast kernel (programmatic dependent), this
+            // grid may start while the copies are being written: x read as
+            // the caller stored it (fp32, no copy) loads at once, B and any
+            // copy of x after the cast has finished.
+            const bool x_early = X3 && p.x_copy == 0;
+            if (x_early)
+                for (int s = 0; s < kStX && s < n_st; ++s) load_x(s);
+            grid_dep_wait();
             for (int s = 0; s < kStB && s < n_st; ++s) load_b(s);
-            for (int s = 0; s < kStX && s < n_st; ++s) load_x(s);
+            if (!x_early)
+                for (int s = 0; s < kStX && s < n_st; ++s) load_x(s);
             for (int s = 0; s < n_st && ok; ++s) {
                 const int st = s % kStB;
                 if (!(ok = mbar_wait(&bars.b_full[st], (uint32_t)((s / kStB) & 1), kWaitBudget))) break;
@@ -2035,19 +2044,27 @@ int configure_tc(const helix_ctx*) {
     return cudaFuncSetAttribute(tc_state_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_STATE_X3);
 }
 
-int launch_tc_state_pass(const helix_ctx* ctx, const ScanParams& p, int runs, bool x3, void* stream) {
+int launch_tc_state_pass(const helix_ctx* ctx, const ScanParams& p, int runs, bool x3, bool after_cast,
+                         void* stream) {
     auto fn = reinterpret_cast<EncodeFn>(ctx->encode_tiled);
     if (!fn) return cudaErrorNotSupported;
     TcMaps maps;
     if (!make_state_maps(fn, &maps, p, x3)) return cudaErrorInvalidValue;
     const int64_t per_run = (int64_t)p.n_pslab * p.H * p.S * p.n_half;
-    const unsigned grid = (unsigned)(per_run * runs);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (x3)
-        tc_state_kernel<true><<<grid, kStThreads, SMEM_STATE_X3, st>>>(maps, p, runs);
-    else
-        tc_state_kernel<false><<<grid, kStThreads, SMEM_STATE, st>>>(maps, p, runs);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(per_run * runs));
+    cfg.blockDim = dim3(kStThreads);
+    cfg.dynamicSmemBytes = x3 ? SMEM_STATE_X3 : SMEM_STATE;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    // behind our own cast kernel only: a programmatic dependent may start
+    // before its predecessor ends, which only that kernel allows for
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = after_cast ? 1 : 0;
+    return x3 ? cudaLaunchKernelEx(&cfg, tc_state_kernel<true>, maps, p, runs)
+              : cudaLaunchKernelEx(&cfg, tc_state_kernel<false>, maps, p, runs);
 }
 
 int launch_tc_carry(const ScanParams& p, bool after_ours, void* stream) {
@@ -2070,8 +2087,9 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const char* only = std::getenv("HELIX_ONLY_PASS");
     ScanParams p = p_in;
+    const bool cast_ran = pl.cast && !pl.states_ready && (!only || *only == 'X');
     if (pl.cast) {  // F32-stored x, B, C: the kernels below read bf16 copies
-        const int e = launch_cast(ctx, pl, &p, stream, !pl.states_ready && (!only || *only == 'X'));
+        const int e = launch_cast(ctx, pl, &p, stream, cast_ran);
         if (e != cudaSuccess) return e;
     }
     TcMaps maps;
@@ -2088,7 +2106,7 @@ int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, void
     const bool do_a = (!only || *only == 'A') && !pl.states_ready;
     const bool do_c = !only || *only == 'C';
     if (pl.need_state_kernel && do_a) {
-        const int e = launch_tc_state_pass(ctx, p, pl.state_runs, false, stream);
+        const int e = launch_tc_state_pass(ctx, p, pl.state_runs, false, cast_ran, stream);
         if (e != cudaSuccess) return e;
     }
     const bool do_b = !only || *only == 'B';
@@ -2146,7 +2164,7 @@ int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_i
         const int e = launch_cast(ctx, pl, &p, stream, true);
         if (e != cudaSuccess) return e;
     }
-    return launch_tc_state_pass(ctx, p, pl.state_runs, false, stream);
+    return launch_tc_state_pass(ctx, p, pl.state_runs, false, pl.cast, stream);
 }
 
 int fault_word_address(unsigned** out) {

@@ -683,7 +683,8 @@ int launch_tc3(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, voi
     ScanParams p = p_in;
     // x, B, C as bf16 hi | lo copies (already in the scratch when the shard
     // state pass left them there)
-    int e = launch_cast(ctx, pl, &p, stream, !pl.states_ready && (!only || *only == 'X'));
+    const bool cast_ran = !pl.states_ready && (!only || *only == 'X');
+    int e = launch_cast(ctx, pl, &p, stream, cast_ran);
     if (e != cudaSuccess) return e;
     TcMaps maps;
     if (!make_tc3_maps(fn, &maps, p)) return cudaErrorInvalidValue;
@@ -693,7 +694,7 @@ int launch_tc3(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_in, voi
     const bool state_ran = pl.need_state_kernel && do_a;
     const bool carry_ran = pl.need_state_kernel && do_b;
     if (state_ran) {
-        e = launch_tc_state_pass(ctx, p, pl.state_runs, true, stream);
+        e = launch_tc_state_pass(ctx, p, pl.state_runs, true, cast_ran, stream);
         if (e != cudaSuccess) return e;
     }
     if (carry_ran) {
@@ -727,7 +728,7 @@ int launch_tc3_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p_
     ScanParams p = p_in;
     const int e = launch_cast(ctx, pl, &p, stream, true);
     if (e != cudaSuccess) return e;
-    return launch_tc_state_pass(ctx, p, pl.state_runs, true, stream);
+    return launch_tc_state_pass(ctx, p, pl.state_runs, true, true, stream);
 }
 
 }  // namespace hx

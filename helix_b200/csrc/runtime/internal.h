@@ -209,9 +209,11 @@ int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, 
 int launch_tc3_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 // kernels/scan_tc.cu, shared with scan_tc3.cu: the tcgen05 state kernel over
 // `runs` runs (x3: the three-product mode, reading fp32 x and the low halves
-// of B from p.cast_bl), and the carry kernel (programmatic dependent of the
-// previous kernel when after_ours).
-int launch_tc_state_pass(const helix_ctx* ctx, const ScanParams& p, int runs, bool x3, void* stream);
+// of B from p.cast_bl; a programmatic dependent of the cast kernel when
+// after_cast), and the carry kernel (programmatic dependent of the previous
+// kernel when after_ours).
+int launch_tc_state_pass(const helix_ctx* ctx, const ScanParams& p, int runs, bool x3, bool after_cast,
+                         void* stream);
 int launch_tc_carry(const ScanParams& p, bool after_ours, void* stream);
 // kernels/scan_cast.cu: when `run`, enqueues the copies of x (Plan::x_copy),
 // B and C into p->cast_*; then points *p at the copies (dense strides).
