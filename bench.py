@@ -46,7 +46,8 @@ sys.path.insert(0, str(ROOT))
 METRIC = "SSD prefill tok/s and % of TC/HBM roofline, L=8192 H64 P64 N128, 1/2/4/8 B200"
 UNIT = "tok/s"
 BACKENDS = {"auto": 0, "sgmma": 1, "mpp": 2, "ref": 3}  # helix_backend
-FAMILIES = {0: "exact fp32 cuda-core", 1: "tcgen05 bf16", 2: "tcgen05 fp32-class (bf16 hi+lo, three products)"}
+FAMILIES = {0: "exact fp32 cuda-core", 1: "tcgen05 bf16", 2: "tcgen05 fp32-class (bf16 hi+lo, three products)",
+            3: "diagonal-A recurrence (cuda-core fp32)"}
 
 
 def parse():
@@ -71,6 +72,9 @@ def parse():
     ap.add_argument("--lsplit", type=int, default=0,
                     help="token shards per head shard: run the L-split mesh on --config (default c5)")
     ap.add_argument("--seqs", type=int, default=0, help="override the config's sequence count (L-split mode)")
+    ap.add_argument("--a-form", default="scalar", choices=["scalar", "diag"],
+                    help="diag: one decay rate per (head, state) (Mamba-1), the recurrence kernels; "
+                         "each head's rate times a seeded factor in [1/4, 4] per state")
     return ap.parse_args()
 
 
@@ -412,8 +416,13 @@ def main():
                   "bf16" if x.dtype == torch.bfloat16 else "f32")
     y = torch.empty(x.shape, dtype=torch.float32, device=dev)
     s1 = torch.empty_like(s0)
+    if a.a_form == "diag":
+        gen = torch.Generator(device=dev).manual_seed(4242)
+        f = torch.exp((torch.rand(A.shape[0], shape.N, device=dev, generator=gen) * 2 - 1) * torch.log(
+            torch.tensor(4.0, device=dev)))
+        A = (A[:, None] * f).contiguous()
     d = helix_b200.desc_from_tensors(x, dt, B, s0, y, multipass=True, compute=a.compute,
-                                     backend=BACKENDS[a.backend])
+                                     backend=BACKENDS[a.backend], A=A)
     if not ctx.supported(d):
         raise SystemExit(f"descriptor unsupported: {ctx.last_error()}")
     info = ctx.plan_info(d)
@@ -471,7 +480,7 @@ def main():
         launches = (2 if has_runs else 0) + 2 * n_half
     elif info.family == 2:
         launches = (2 if has_runs else 0) + n_half
-    else:
+    else:  # exact fp32 and diagonal-A families: state kernel when runs are carried, output kernel
         launches = (1 if has_runs else 0) + 1
     n_cast = cast_launches(ctx, d)
     launches += n_cast
@@ -505,6 +514,20 @@ def main():
         passes["output"]["mma_flops"] = mma
         passes["output"]["mma_tflops"] = mma / (ms_pass["output"] * 1e-3) / 1e12
         passes["output"]["mma_tensor_frac"] = passes["output"]["mma_tflops"] / tc
+    if info.family == 3:
+        # the recurrence: per (token, head, channel, state) one multiply and
+        # two fused multiply-adds in the output pass (5 flops), one multiply
+        # and one in the state pass (3), against the nominal CUDA-core fp32
+        # rate (148 SMs x 128 lanes x 2 flops x the max SM clock)
+        upd = shape.S * shape.L * shape.H * shape.P * shape.N
+        fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        for name, fl, tok in (("output", 5.0, shape.L), ("state", 3.0, min(shape.L, info.state_runs * info.run_tokens))):
+            if name in passes:
+                tf = fl * upd * tok / shape.L / (ms_pass[name] * 1e-3) / 1e12
+                passes[name].pop("tflops", None)
+                passes[name].pop("tensor_frac", None)
+                passes[name]["fp32_tflops"] = tf
+                passes[name]["fp32_frac_of_nominal"] = tf / fp32_peak
     achieved = out_bytes / (ms_pass["output"] * 1e-3) / 1e9
     traffic = None  # DRAM bytes per launch of the output kernel, from the committed ncu capture
     tj = ROOT / "profiles" / "ncu_traffic.json"
@@ -610,7 +633,7 @@ def main():
         "data": "synthetic (seeded, BASELINE distributions; random A, B, C, x, dt)",
         "config": {"workload": f"{a.config}: S={gshape.S} L={gshape.L} H={gshape.H} P={gshape.P} "
                                f"N={gshape.N} G={gshape.G}, x/B/C {shape.io}, dt/A/s0/y/s1 f32, multipass; "
-                               f"{layout}",
+                               f"{layout}" + ("; diagonal A (one rate per (head, state))" if a.a_form == "diag" else ""),
                    "l2": "flushed before every timed step (256 MiB write, untimed)",
                    "compute": a.compute, "runs_plan_scratch_bytes": nbytes,
                    "backend": a.backend,
@@ -629,7 +652,7 @@ def main():
     }
     if e2e:
         line["e2e"] = e2e
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+    if rank == 0 and world == 1 and not a.no_cpu_baseline and a.a_form == "scalar":
         line["cpu_baseline"] = cpu_baseline(gshape, a.cpu_sample_tokens)
         line["cpu_baseline_chunked"] = cpu_baseline(gshape, a.cpu_sample_tokens, "chunked")
     if rank == 0:

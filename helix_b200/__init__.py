@@ -118,10 +118,12 @@ class Context:
 
 
 def desc_from_tensors(x, dt, B, s0, y=None, *, multipass: bool = True, compute: str = "auto",
-                      backend: int = abi.HELIX_BACKEND_AUTO) -> abi.ScanDesc:
+                      backend: int = abi.HELIX_BACKEND_AUTO, A=None) -> abi.ScanDesc:
     """Descriptor for torch tensors laid out as in helix.h:
     x (S, L, H, P), dt (S, L, H), B and C (S, L, G, N), s0 (S, H, P, N),
-    y (S, L, H, P).  Strides are taken from the tensors, so views work."""
+    y (S, L, H, P).  Strides are taken from the tensors, so views work.
+    A, if given, sets the decay form: (H,) scalar per head, (H, N) one rate
+    per (head, state) (HELIX_A_DIAG_PER_CHANNEL, rows A.stride(0) apart)."""
     import torch
     S, L, H, P = x.shape
     G, N = B.shape[2], B.shape[3]
@@ -139,6 +141,14 @@ def desc_from_tensors(x, dt, B, s0, y=None, *, multipass: bool = True, compute: 
     d.compute_dtype = abi.HELIX_BF16 if compute == "bf16" else abi.HELIX_F32
     d.backend = backend
     d.multipass = multipass
+    if A is not None:
+        if A.dim() == 2:
+            if A.stride(1) != 1:
+                raise ValueError("a per-state A needs unit stride along d_state")
+            d.a_form = abi.HELIX_A_DIAG_PER_CHANNEL
+            d.s_a = A.stride(0)
+        else:
+            d.s_a = A.stride(0)
     return d
 
 
@@ -157,7 +167,7 @@ def scan(x, dt, A, B, Cm, s0, ids=None, *, multipass: bool = True, compute: str 
         ctx = _default_ctx.get(dev) or _default_ctx.setdefault(dev, Context(dev))
     y = torch.empty(x.shape, dtype=torch.float32, device=x.device)
     s1 = torch.empty(s0.shape, dtype=torch.float32, device=x.device)
-    d = desc_from_tensors(x, dt, B, s0, y, multipass=multipass, compute=compute, backend=backend)
+    d = desc_from_tensors(x, dt, B, s0, y, multipass=multipass, compute=compute, backend=backend, A=A)
     if Cm.stride() != B.stride():
         d.s_c[:] = list(Cm.stride()[1:]); d.seq_c = Cm.stride(0)
     nbytes = ctx.scratch_size(d)
@@ -192,7 +202,7 @@ def shard_state(x, dt, A, B, Cm, *, compute: str = "auto", backend: int = abi.HE
     N = B.shape[3]
     state = torch.empty((S, H, P, N), dtype=torch.float32, device=x.device)
     log_decay = torch.empty((S, H), dtype=torch.float32, device=x.device)
-    d = desc_from_tensors(x, dt, B, state, None, multipass=True, compute=compute, backend=backend)
+    d = desc_from_tensors(x, dt, B, state, None, multipass=True, compute=compute, backend=backend, A=A)
     if Cm.stride() != B.stride():
         d.s_c[:] = list(Cm.stride()[1:]); d.seq_c = Cm.stride(0)
     nbytes = ctx.shard_state_scratch_size(d)
@@ -214,7 +224,7 @@ def scan_shard(x, dt, A, B, Cm, carry, scratch, *, compute: str = "auto", backen
     ctx = _ctx_for(x, ctx)
     y = torch.empty(x.shape, dtype=torch.float32, device=x.device)
     s1 = torch.empty(carry.shape, dtype=torch.float32, device=x.device)
-    d = desc_from_tensors(x, dt, B, carry, y, multipass=True, compute=compute, backend=backend)
+    d = desc_from_tensors(x, dt, B, carry, y, multipass=True, compute=compute, backend=backend, A=A)
     if Cm.stride() != B.stride():
         d.s_c[:] = list(Cm.stride()[1:]); d.seq_c = Cm.stride(0)
     st = ctx.encode_shard(d, carry, x, dt, A, B, Cm, y, s1, scratch, stream=stream)

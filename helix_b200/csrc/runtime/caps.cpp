@@ -61,7 +61,11 @@ size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 // so single pass (no scratch) takes the exact fp32 family, as does the
 // three-product family's request with bf16-stored x, B, C (the reference's
 // bf16 Pass C needs its multipass staging too, src/runtime/caps.mm:59-72).
+// Diagonal A (declined by the reference, caps.mm:121-123) takes the
+// recurrence kernels of kernels/scan_diag.cu whatever the backend and
+// precision asked for: they compute in fp32.
 Path select_path(const helix_scan_desc& d) {
+    if (d.a_form == HELIX_A_DIAG_PER_CHANNEL) return kPathDiag;  // every backend
     if (d.backend == HELIX_BACKEND_REF) return kPathSimtF32;
     const bool bf16 = d.backend == HELIX_BACKEND_MPP || (d.backend != HELIX_BACKEND_SGMMA && d.compute_dtype == HELIX_BF16);
     if (bf16) return d.io_dtype == HELIX_F32 && !d.multipass ? kPathSimtF32 : kPathTcBf16;
@@ -76,9 +80,9 @@ bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why) 
     if (!ctx) return no("null context");
     if (!positive_dims(d)) return no("non-positive dimension");
     if (d.n_head % d.n_group != 0) return no("n_head not a multiple of n_group");
-    // Only the scalar decay admits the chunked reassociation
-    // (reference src/runtime/caps.mm:121-123).
-    if (d.a_form != HELIX_A_SCALAR_PER_HEAD) return no("diagonal A is not accelerated");
+    // Only the scalar decay admits the chunked reassociation (reference
+    // src/runtime/caps.mm:121-123); diagonal A runs the recurrence itself.
+    if (d.a_form != HELIX_A_SCALAR_PER_HEAD && d.a_form != HELIX_A_DIAG_PER_CHANNEL) return no("unknown a_form");
     if (d.io_dtype != HELIX_F32 && d.io_dtype != HELIX_BF16) return no("io_dtype must be F32 or BF16");
     if (d.compute_dtype != HELIX_F32 && d.compute_dtype != HELIX_BF16)
         return no("compute_dtype must be F32 or BF16");
@@ -92,6 +96,11 @@ bool supported_impl(helix_ctx* ctx, const helix_scan_desc& d, std::string* why) 
             ((d.n_tok + kRunQuantum - 1) / kRunQuantum) > (int64_t)INT32_MAX)
         return no("problem too large for one launch");
 
+    if (select_path(d) == kPathDiag) {
+        // four state groups of up to 64 states per thread
+        if (d.d_state > 256) return no("diagonal-A path needs d_state <= 256");
+        return true;
+    }
     if (select_path(d) == kPathSimtF32) {
         if (d.d_state % 8 != 0 || d.d_state > 256) return no("fp32 path needs d_state % 8 == 0 and <= 256");
         return true;
@@ -227,7 +236,9 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
     Plan pl;
     pl.path = select_path(d);
     const bool tc = pl.path == kPathTcBf16 || pl.path == kPathTcX3;
-    pl.cs = tc ? 128 : (d.d_state <= 128 ? 64 : 32);
+    const bool diag = pl.path == kPathDiag;
+    // chunk: the output kernel's token block (diagonal A: tokens staged per tile)
+    pl.cs = tc ? 128 : diag ? 32 : (d.d_state <= 128 ? 64 : 32);
     pl.n_pslab = (d.head_dim + kSlab - 1) / kSlab;
 
     const int blocks = (d.n_tok + kRunQuantum - 1) / kRunQuantum;  // 128-token blocks
@@ -244,8 +255,11 @@ Plan make_plan(const helix_ctx* ctx, const helix_scan_desc& d) {
         } else if (pl.path == kPathTcX3) {
             tc_split(d, blocks, n_sm, max_runs, 1, kStateCtasPerSmX3, 4, &run_blocks, &out_k);
         } else {
-            // Enough CTAs in the output kernel to cover every SM a few times.
-            const int64_t units = (int64_t)d.n_seq * d.n_head * pl.n_pslab;
+            // Enough CTAs in the output kernel to cover every SM a few times
+            // (diagonal A: one CTA per 64 (head, channel) rows of a group).
+            const int64_t units = diag ? (int64_t)d.n_seq * d.n_group *
+                                             (((int64_t)(d.n_head / d.n_group) * d.head_dim + 63) / 64)
+                                       : (int64_t)d.n_seq * d.n_head * pl.n_pslab;
             const int64_t target = 4 * (int64_t)n_sm;
             int n_runs = (int)std::min<int64_t>(blocks, std::max<int64_t>(1, (target + units - 1) / units));
             n_runs = std::min(n_runs, max_runs);
@@ -317,6 +331,7 @@ extern "C" const char* helix_ctx_backend_desc(helix_ctx* ctx, const helix_scan_d
     switch (hx::select_path(*d)) {
         case hx::kPathTcBf16: return "tcgen05 (bf16 operands, fp32 accumulators and state)";
         case hx::kPathTcX3: return "tcgen05 (fp32 operands as bf16 hi+lo, three products, fp32 accumulators and state)";
+        case hx::kPathDiag: return "cuda-core (diagonal A: per-state decay recurrence, fp32)";
         default: return "cuda-core (exact fp32)";
     }
 }

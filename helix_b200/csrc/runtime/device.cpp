@@ -98,7 +98,7 @@ extern "C" helix_status helix_ctx_create(helix_ctx** out, void* device, const ch
 
     {
         DeviceGuard g(dev);
-        if (hx::configure_simt(ctx) != cudaSuccess) {
+        if (hx::configure_simt(ctx) != cudaSuccess || hx::configure_diag(ctx) != cudaSuccess) {
             hx::set_error(nullptr, std::string("configuring fp32 kernels failed: ") +
                                        cudaGetErrorString(cudaGetLastError()));
             delete ctx;

@@ -176,6 +176,7 @@ helix_status run_call(helix_ctx* ctx, const Plan& pl, const ScanParams& p, void*
     if (dev_prev != ctx->device) cudaSetDevice(ctx->device);
     const int rc = pl.path == kPathTcBf16 ? launch_tc(ctx, pl, p, stream)
                    : pl.path == kPathTcX3 ? launch_tc3(ctx, pl, p, stream)
+                   : pl.path == kPathDiag ? launch_diag(ctx, pl, p, stream)
                                           : launch_simt(ctx, pl, p, stream);
     if (dev_prev >= 0 && dev_prev != ctx->device) cudaSetDevice(dev_prev);
     if (rc != cudaSuccess) {

@@ -45,6 +45,7 @@ enum Path : int {
     kPathTcBf16  = 1,   // tcgen05 kernels, bf16 operands, fp32 state
     kPathTcX3    = 2,   // tcgen05 kernels, three-product bf16 split of fp32
                         // operands (hi.hi + hi.lo + lo.hi), fp32 state
+    kPathDiag    = 3,   // diagonal A: the per-state recurrence on CUDA cores, fp32
 };
 
 // How one descriptor is executed.  A pure function of (ctx, desc, env):
@@ -203,6 +204,7 @@ bool states_overlap(const helix_scan_desc& d, const void* s0, const void* s1);
 int launch_simt(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 int launch_tc(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 int launch_tc3(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
+int launch_diag(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 // State kernel over every run of the plan (p.agg / p.lam for all n_runs).
 int launch_simt_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
 int launch_tc_states(const helix_ctx* ctx, const Plan& pl, const ScanParams& p, void* stream);
@@ -231,6 +233,7 @@ int launch_carry_combine(const ScanParams& p, const float* states, const float* 
 int configure_simt(const helix_ctx* ctx);
 int configure_tc(const helix_ctx* ctx);
 int configure_tc3(const helix_ctx* ctx);
+int configure_diag(const helix_ctx* ctx);
 int read_tc_fault(unsigned* code);
 // Device address of the fault word on the current device.
 int fault_word_address(unsigned** out);

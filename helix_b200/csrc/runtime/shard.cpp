@@ -66,6 +66,11 @@ extern "C" helix_status helix_scan_shard_state(helix_ctx* ctx, void* stream, con
         hx::set_error(ctx, why);
         return HELIX_ERR_UNSUPPORTED_SHAPE;
     }
+    if (m.a_form != HELIX_A_SCALAR_PER_HEAD) {
+        // a shard's decay is one scalar per (seq, head) only for scalar A
+        hx::set_error(ctx, "token sharding needs scalar A");
+        return HELIX_ERR_UNSUPPORTED_SHAPE;
+    }
     const hx::Plan pl = hx::make_shard_plan(ctx, m);
     if ((reinterpret_cast<uintptr_t>(at<char>(scratch)) & 255) != 0) {
         hx::set_error(ctx, "scratch must be 256-byte aligned");
@@ -117,6 +122,10 @@ extern "C" helix_status helix_scan_carry_combine(helix_ctx* ctx, void* stream, c
         hx::set_error(ctx, "bad state shape or innermost state stride != 1");
         return HELIX_ERR_UNSUPPORTED_SHAPE;
     }
+    if (d->a_form != HELIX_A_SCALAR_PER_HEAD) {
+        hx::set_error(ctx, "token sharding needs scalar A");
+        return HELIX_ERR_UNSUPPORTED_SHAPE;
+    }
     if (hx::states_overlap(*d, at<char>(s0), at<char>(carry))) {
         hx::set_error(ctx, "s0 and carry overlap");
         return HELIX_ERR_INVALID_ARG;
@@ -151,6 +160,11 @@ extern "C" helix_status helix_scan_encode_shard(helix_ctx* ctx, void* stream, co
     std::string why;
     if (!hx::supported_impl(ctx, m, &why)) {
         hx::set_error(ctx, why);
+        return HELIX_ERR_UNSUPPORTED_SHAPE;
+    }
+    if (m.a_form != HELIX_A_SCALAR_PER_HEAD) {
+        // a shard's decay is one scalar per (seq, head) only for scalar A
+        hx::set_error(ctx, "token sharding needs scalar A");
         return HELIX_ERR_UNSUPPORTED_SHAPE;
     }
     hx::Plan pl = hx::make_plan(ctx, m);

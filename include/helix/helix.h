@@ -69,9 +69,13 @@ typedef enum {
 } helix_dtype;
 
 typedef enum {
-    /* One decay scalar per head: Mamba-2 / SSD.  The only form accelerated. */
+    /* One decay scalar per head: Mamba-2 / SSD (the chunked tensor-core
+     * families). */
     HELIX_A_SCALAR_PER_HEAD = 0,
-    /* One decay per (head, state): Mamba-1.  Declined by helix_scan_supported. */
+    /* One decay per (head, state), A[h * s_a + n]: Mamba-1.  The reference
+     * declines it; here it runs the per-state recurrence on the CUDA cores in
+     * fp32 whatever the backend and compute_dtype (d_state <= 256), and the
+     * token-shard entry points of helix_ext.h decline it. */
     HELIX_A_DIAG_PER_CHANNEL = 1,
 } helix_a_form;
 

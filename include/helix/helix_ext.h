@@ -65,7 +65,8 @@ helix_status helix_scan_encode_static(helix_ctx*             ctx,
  * helix_scan_supported rejects. */
 typedef struct helix_plan_info {
     int32_t  family;         /* 0: exact fp32 CUDA-core kernels, 1: tcgen05 bf16,
-                                2: tcgen05 three-product (fp32-class) */
+                                2: tcgen05 three-product (fp32-class),
+                                3: diagonal-A recurrence (CUDA cores, fp32) */
     int32_t  chunk;          /* tokens per chunk of the output kernel */
     int32_t  run_tokens;     /* tokens per run */
     int32_t  n_runs;         /* runs per sequence */

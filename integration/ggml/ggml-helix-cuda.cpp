@@ -24,9 +24,10 @@
 //   dst         y, then the final state at byte offset nelements(x) * 4
 //
 // Gates kept from the reference bridge: one snapshot (K == 1), all F32,
-// scalar A ({1, n_head}; a per-channel A is declined by helix), n_head a
-// multiple of n_group, and at least GGML_HELIX_MIN_TOKENS tokens -- below
-// that the fixed cost of the chunked scan's launches loses to ggml's own
+// n_head a multiple of n_group, and at least GGML_HELIX_MIN_TOKENS tokens.
+// Unlike the reference's hook, a per-state A ({d_state, n_head}, Mamba-1)
+// is passed on as HELIX_A_DIAG_PER_CHANNEL and served.  Below the token gate
+// the fixed cost of the chunked scan's launches loses to ggml's own
 // per-token kernel (the crossover is measured on B200 by measure_gate.py).
 // ggml applies no clamp to softplus(dt), so neither does the descriptor.
 //
@@ -198,7 +199,7 @@ bool build_desc(const ggml_tensor * op, helix_scan_desc * d) {
     if (src3->ne[0] == 1) {
         d->a_form = HELIX_A_SCALAR_PER_HEAD;
     } else if (src3->ne[0] == d_state) {
-        d->a_form = HELIX_A_DIAG_PER_CHANNEL;  // declined by helix_scan_supported
+        d->a_form = HELIX_A_DIAG_PER_CHANNEL;  // the diagonal-A recurrence kernels
     } else {
         return false;
     }

@@ -130,6 +130,17 @@ class Oracle(_Base):
                                      *[_f(a) for a in (s0, x, dt, A, B, Cm)])
         return dict(s0=s0, x=x, dt=dt, A=A, B=B, C=Cm)
 
+    def harness_problem_diag(self, L, S, H, P, N, G, seed, long_memory=False):
+        """The harness problem with diagonal A (one rate per (head, state),
+        helix.h HELIX_A_DIAG_PER_CHANNEL, read as A[h * d_state + n]): each
+        head's harness rate times a factor drawn log-uniform in [1/4, 4]
+        (numpy PCG64 seeded with `seed`), so both memory regimes keep their
+        decay scale.  The reference's harness has no diagonal-A generator."""
+        prob = self.harness_problem(L, S, H, P, N, G, seed, long_memory)
+        f = np.exp(np.random.default_rng(seed).uniform(-np.log(4.0), np.log(4.0), (H, N)))
+        prob["A"] = (prob["A"][:, None] * f).astype(np.float32)
+        return prob
+
     def carry_chain(self, s0, agg, lam):
         """carry[k] = state entering slice k (see helix_oracle.c)."""
         K = agg.shape[0]
@@ -159,6 +170,13 @@ class Reference(_Base):
 
     def desc_size(self) -> int:
         return int(self.lib.ref_desc_size())
+
+
+def diag_desc(d):
+    """Switches a dense descriptor to diagonal A (A dense [n_head][d_state])."""
+    d.a_form = 1  # HELIX_A_DIAG_PER_CHANNEL
+    d.s_a = d.d_state
+    return d
 
 
 def available_reference() -> bool:

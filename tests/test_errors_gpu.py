@@ -39,12 +39,12 @@ def _untouched(t):
     return bool(torch.isnan(t["y"]).all()) and bool(torch.isnan(t["s1"]).all())
 
 
-def test_unsupported_diagonal_a(ctx, cuda):
+def test_unsupported_a_form(ctx, cuda):
     t = _problem(cuda)
     d = _desc(t, multipass=False)
-    d.a_form = abi.HELIX_A_DIAG_PER_CHANNEL
+    d.a_form = 7  # neither helix_a_form value
     assert not ctx.supported(d)
-    assert "diagonal" in ctx.last_error()
+    assert "a_form" in ctx.last_error()
     assert _enc(ctx, d, t) == abi.HELIX_ERR_UNSUPPORTED_SHAPE
     assert ctx.backend_desc(d).startswith("declined")
     assert _untouched(t)
@@ -163,9 +163,9 @@ def test_error_strings_per_thread_and_freed_with_context(cuda):
     t = _problem(cuda)
     a = helix_b200.Context(0)
     d = _desc(t, multipass=False)
-    d.a_form = abi.HELIX_A_DIAG_PER_CHANNEL
+    d.a_form = 7
     assert not a.supported(d)
-    assert "diagonal" in a.last_error()
+    assert "a_form" in a.last_error()
     seen = {}
     th = threading.Thread(target=lambda: seen.setdefault("other", a.last_error()))
     th.start()

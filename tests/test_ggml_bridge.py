@@ -71,11 +71,10 @@ def _op(t, L, S, H, P, N, G, K=1, a_diag=False, x_type=GGML_F32):
 def _tensors(oracle, L, S, H, P, N, G, a_diag=False):
     import torch
     dev = torch.device("cuda:0")
-    prob = oracle.harness_problem(L, S, H, P, N, G, 4242, True)
+    make = oracle.harness_problem_diag if a_diag else oracle.harness_problem
+    prob = make(L, S, H, P, N, G, 4242, True)  # diagonal A: [H][N]
     prob["s0"] = np.random.default_rng(1).normal(0, 0.1, prob["s0"].shape).astype(np.float32)
     t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in prob.items()}
-    if a_diag:
-        t["A"] = t["A"][:, None].expand(H, N).contiguous()
     t["ids"] = torch.arange(S, dtype=torch.int32, device=dev).flip(0).contiguous()  # reversed rows
     t["dst"] = torch.full((S * L * H * P + S * H * P * N,), float("nan"), device=dev)
     return prob, t
@@ -104,13 +103,36 @@ def test_bridge_serves_ssm_scan(bridge, oracle, shape):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("case", ["K2", "f16_x", "diag_A", "short"])
+@pytest.mark.parametrize("shape", [(300, 2, 8, 64, 128, 2), (200, 2, 96, 1, 16, 1)], ids=["mamba2_like", "mamba1_like"])
+def test_bridge_serves_diagonal_a(bridge, oracle, shape):
+    """A {d_state, n_head} (one rate per state): the reference's hook
+    declines it; this one runs the diagonal-A recurrence kernels."""
+    import torch
+    from oracle.oracle import diag_desc
+    L, S, H, P, N, G = shape
+    prob, t = _tensors(oracle, *shape, a_diag=True)
+    dst = _op(t, *shape, a_diag=True)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert bridge.ggml_cuda_op_ssm_scan_helix(C.c_void_p(stream), 0, C.byref(dst))
+    torch.cuda.synchronize()
+    out = t["dst"].cpu().numpy()
+    y = out[: S * L * H * P].reshape(S, L, H, P)
+    s1 = out[S * L * H * P:].reshape(S, H, P, N)
+    ids = t["ids"].cpu().numpy()
+    y_ref, s_ref = oracle.scan(diag_desc(oracle.desc_init(*shape)),
+                               *[prob[k] for k in ("s0", "x", "dt", "A", "B", "C")], ids=ids)
+    for got, want in ((y, y_ref), (s1, s_ref)):
+        c = compare(got, want, X3_REL, X3_ABS)
+        assert c["ok"] and c["rel_l2"] <= X3_RL2, c
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", ["K2", "f16_x", "short"])
 def test_bridge_declines_what_the_reference_declines(bridge, oracle, case):
     import torch
     shape = (31 if case == "short" else 300, 1, 4, 64, 128, 1)
-    _, t = _tensors(oracle, *shape, a_diag=case == "diag_A")
-    dst = _op(t, *shape, K=2 if case == "K2" else 1, a_diag=case == "diag_A",
-              x_type=GGML_OTHER if case == "f16_x" else GGML_F32)
+    _, t = _tensors(oracle, *shape)
+    dst = _op(t, *shape, K=2 if case == "K2" else 1, x_type=GGML_OTHER if case == "f16_x" else GGML_F32)
     stream = torch.cuda.current_stream().cuda_stream
     assert not bridge.ggml_cuda_op_ssm_scan_helix(C.c_void_p(stream), 0, C.byref(dst))
     torch.cuda.synchronize()

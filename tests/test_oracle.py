@@ -143,3 +143,68 @@ def test_carry_chain_is_the_sequential_state(oracle):
                                    np.stack([a[0, h] for a in aggs]), np.array([l[h] for l in lams]))
         final = np.exp(lams[-1][h]) * carry[-1] + aggs[-1][0, h].ravel()
         assert compare(final, s_full[0, h].ravel(), 1e-5, 1e-7)["ok"]
+
+
+# ---- diagonal A (HELIX_A_DIAG_PER_CHANNEL) ----------------------------------
+
+GOLDEN_DIAG = sorted((Path(__file__).parent / "golden" / "diag").glob("*.npz"))
+
+
+def test_golden_diag_files_present():
+    assert len(GOLDEN_DIAG) >= 5
+
+
+@pytest.mark.parametrize("path", GOLDEN_DIAG, ids=[p.stem for p in GOLDEN_DIAG])
+def test_golden_diag(oracle, path):
+    """Diagonal-A outputs of the reference's own fp64 oracle (its scan reads
+    A[h * s_a + n] for this form, src/reference/scan_ref.cpp:27-29)."""
+    from oracle.oracle import diag_desc
+    z, (L, S, H, P, N, G) = _load(path)
+    prob = oracle.harness_problem_diag(L, S, H, P, N, G, int(z["seed"]), bool(z["long_memory"]))
+    assert _digest(prob) == str(z["inputs_sha256"]), "restated input generator drifted"
+    ids = z["ids"] if z["ids"].size else None
+    y, s1 = oracle.scan(diag_desc(oracle.desc_init(L, S, H, P, N, G)), *_args(prob), ids=ids)
+    np.testing.assert_array_equal(y, z["y"])
+    np.testing.assert_array_equal(s1, z["s1"])
+
+
+DIAG_SHAPES = [(1, 1, 1, 64, 128, 1), (65, 1, 2, 64, 128, 1), (130, 2, 64, 1, 16, 1),
+               (100, 1, 4, 48, 64, 2), (64, 1, 2, 64, 256, 1)]
+
+
+@pytest.mark.parametrize("long_mem", [False, True], ids=["short", "long"])
+@pytest.mark.parametrize("shape", DIAG_SHAPES, ids=["L{}S{}H{}P{}N{}G{}".format(*s) for s in DIAG_SHAPES])
+def test_diag_restatement_vs_reference(oracle, reference, shape, long_mem):
+    from oracle.oracle import diag_desc
+    prob = oracle.harness_problem_diag(*shape, 12345, long_mem)
+    y_o, s_o = oracle.scan(diag_desc(oracle.desc_init(*shape)), *_args(prob))
+    y_r, s_r = reference.scan(diag_desc(reference.desc_init(*shape)), *_args(prob))
+    np.testing.assert_array_equal(y_o, y_r)
+    np.testing.assert_array_equal(s_o, s_r)
+    # the chunked reassociation has no diagonal form: both decline it
+    y_c, _ = oracle.scan_chunked(diag_desc(oracle.desc_init(*shape)), *_args(prob))
+    assert not np.any(y_c)
+
+
+def test_diag_run_carry_identity(oracle):
+    """Cutting a slice into K runs, scanning each from a zero state and
+    chaining S = exp(A[h][n] D_k) S + agg_k, D_k the run's dt sum, reproduces
+    the uncut final state: the identity the diagonal-A kernels' run carry
+    relies on (A is constant over a run, so a state's decay over it is one
+    exponential of the summed dt)."""
+    from oracle.oracle import diag_desc
+    L, H, P, N, K = 384, 2, 8, 16, 3
+    prob = oracle.harness_problem_diag(L, 1, H, P, N, 1, 4242, True)
+    _, s_full = oracle.scan(diag_desc(oracle.desc_init(L, 1, H, P, N, 1)), *_args(prob))
+    piece = L // K
+    zero = np.zeros_like(prob["s0"])
+    state = prob["s0"][0].astype(np.float64)  # [H][P][N]
+    A = prob["A"].astype(np.float64)          # [H][N]
+    for k in range(K):
+        sl = slice(k * piece, (k + 1) * piece)
+        sub = dict(prob, x=np.ascontiguousarray(prob["x"][:, sl]), dt=np.ascontiguousarray(prob["dt"][:, sl]),
+                   B=np.ascontiguousarray(prob["B"][:, sl]), C=np.ascontiguousarray(prob["C"][:, sl]), s0=zero)
+        _, agg = oracle.scan(diag_desc(oracle.desc_init(piece, 1, H, P, N, 1)), *_args(sub))
+        D = np.log1p(np.exp(prob["dt"][0, sl].astype(np.float64))).sum(0)  # [H]
+        state = np.exp(A * D[:, None])[:, None, :] * state + agg[0].astype(np.float64)
+    assert compare(state.astype(np.float32), s_full[0], 1e-5, 1e-7)["ok"]
