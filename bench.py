@@ -138,58 +138,98 @@ def cpu_baseline(shape, sample_tokens: int, which: str = "scan"):
 
 
 # ---------------------------------------------------------------------------
+def _clock_sampler(bus_id, index, conn, go, stop):
+    """Child process: polls NVML every ~0.2 ms between `go` and `stop`, then
+    sends [(sm_mhz, event_reasons)] and the max SM clock back."""
+    rows, max_mhz = [], None
+    try:
+        import pynvml as nv
+        nv.nvmlInit()
+        try:
+            h = nv.nvmlDeviceGetHandleByPciBusId(bus_id) if bus_id else nv.nvmlDeviceGetHandleByIndex(index)
+        except Exception:
+            h = nv.nvmlDeviceGetHandleByIndex(index)
+        max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        conn.send("ready")
+        go.wait(60)
+        while not stop.is_set():
+            t0 = time.perf_counter()
+            try:
+                rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                             nv.nvmlDeviceGetCurrentClocksEventReasons(h), time.perf_counter() - t0))
+            except Exception:
+                pass
+            time.sleep(0.0002)
+    except Exception:
+        try:
+            conn.send("ready")
+        except Exception:
+            pass
+    conn.send((rows, max_mhz))
+
+
 class Clocks:
-    """SM clock and throttle-reason sampler for the timed region (NVML polled
-    every ~1 ms from a thread; nvidia-smi's cadence is too coarse for a timed
-    region of a few milliseconds)."""
+    """SM clock and throttle-reason sampler for the timed region: NVML polled
+    every ~0.2 ms by a spawned child process (a thread of this process would
+    wait for the GIL while the launching thread enqueues the steps, and
+    nvidia-smi's cadence is too coarse for a region of a few milliseconds).
+    The child starts before the region and samples from `__enter__` to
+    `__exit__`."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, index: int):
-        self.index, self.rows, self.stop = index, [], threading.Event()
-        self.max_mhz = None
+        self.index, self.rows, self.max_mhz, self.proc = index, [], None, None
+        try:
+            import multiprocessing as mp
+            import torch
+            bus = None
+            try:  # same physical GPU as the CUDA ordinal, whatever the visibility mask
+                pr = torch.cuda.get_device_properties(index)
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            except Exception:
+                pass
+            ctx = mp.get_context("spawn")
+            self.conn, child = ctx.Pipe()
+            self.go, self.stop = ctx.Event(), ctx.Event()
+            self.proc = ctx.Process(target=_clock_sampler, args=(bus, index, child, self.go, self.stop), daemon=True)
+            self.proc.start()
+            if not (self.conn.poll(60) and self.conn.recv() == "ready"):
+                raise RuntimeError("sampler did not start")
+        except Exception:
+            self._end()
+
+    def _end(self):
+        if self.proc is not None:
+            self.proc.kill()
+            self.proc = None
 
     def __enter__(self):
-        try:
-            import pynvml as nv
-            nv.nvmlInit()
-            h = None
-            try:  # same physical GPU as the CUDA ordinal, whatever the visibility mask
-                import torch
-                pr = torch.cuda.get_device_properties(self.index)
-                h = nv.nvmlDeviceGetHandleByPciBusId(
-                    f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0")
-            except Exception:
-                h = nv.nvmlDeviceGetHandleByIndex(self.index)
-            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-
-            def loop():
-                while not self.stop.is_set():
-                    try:
-                        self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
-                                          nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
-                    except Exception:
-                        pass
-                    time.sleep(0.001)
-            self.th = threading.Thread(target=loop, daemon=True)
-            self.th.start()
-        except Exception:
-            self.th = None
+        if self.proc is not None:
+            self.go.set()
         return self
 
     def __exit__(self, *a):
+        if self.proc is None:
+            return
         self.stop.set()
-        if self.th:
-            self.th.join(timeout=2)
+        try:
+            if self.conn.poll(10):
+                self.rows, self.max_mhz = self.conn.recv()
+        except Exception:
+            pass
+        self.proc.join(timeout=5)
+        self._end()
 
     def summary(self):
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
         mhz = [r[0] for r in self.rows]
-        reasons = sorted({n for _, m in self.rows for n, bit in self.REASONS.items() if m & bit})
+        reasons = sorted({n for _, m, _ in self.rows for n, bit in self.REASONS.items() if m & bit})
         return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(self.rows), "source": "nvml, ~1 ms poll during the timed steps"}
+                "samples": len(self.rows), "ms_per_sample": 1e3 * statistics.median(r[2] for r in self.rows),
+                "source": "nvml, polled by a child process during the timed steps"}
 
 
 def peaks():
