@@ -138,9 +138,9 @@ def cpu_baseline(shape, sample_tokens: int, which: str = "scan"):
 
 
 # ---------------------------------------------------------------------------
-def _clock_sampler(bus_id, index, conn, go, stop):
-    """Child process: polls NVML every ~0.2 ms between `go` and `stop`, then
-    sends [(sm_mhz, event_reasons)] and the max SM clock back."""
+def _clock_sampler(bus_id, index, conn, stop):
+    """Child process: polls NVML every ~0.2 ms from start-up until `stop`, then
+    sends [(monotonic time, sm_mhz, event_reasons)] and the max SM clock."""
     rows, max_mhz = [], None
     try:
         import pynvml as nv
@@ -151,12 +151,10 @@ def _clock_sampler(bus_id, index, conn, go, stop):
             h = nv.nvmlDeviceGetHandleByIndex(index)
         max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
         conn.send("ready")
-        go.wait(60)
         while not stop.is_set():
-            t0 = time.perf_counter()
             try:
-                rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
-                             nv.nvmlDeviceGetCurrentClocksEventReasons(h), time.perf_counter() - t0))
+                rows.append((time.monotonic(), nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                             nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
             except Exception:
                 pass
             time.sleep(0.0002)
@@ -173,14 +171,15 @@ class Clocks:
     every ~0.2 ms by a spawned child process (a thread of this process would
     wait for the GIL while the launching thread enqueues the steps, and
     nvidia-smi's cadence is too coarse for a region of a few milliseconds).
-    The child starts before the region and samples from `__enter__` to
-    `__exit__`."""
+    The child polls from start-up; the samples kept are those taken between
+    `__enter__` and `__exit__` (CLOCK_MONOTONIC is shared by the processes)."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, index: int):
         self.index, self.rows, self.max_mhz, self.proc = index, [], None, None
+        self.t0 = self.t1 = None
         try:
             import multiprocessing as mp
             import torch
@@ -192,8 +191,8 @@ class Clocks:
                 pass
             ctx = mp.get_context("spawn")
             self.conn, child = ctx.Pipe()
-            self.go, self.stop = ctx.Event(), ctx.Event()
-            self.proc = ctx.Process(target=_clock_sampler, args=(bus, index, child, self.go, self.stop), daemon=True)
+            self.stop = ctx.Event()
+            self.proc = ctx.Process(target=_clock_sampler, args=(bus, index, child, self.stop), daemon=True)
             self.proc.start()
             if not (self.conn.poll(60) and self.conn.recv() == "ready"):
                 raise RuntimeError("sampler did not start")
@@ -206,17 +205,18 @@ class Clocks:
             self.proc = None
 
     def __enter__(self):
-        if self.proc is not None:
-            self.go.set()
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *a):
+        self.t1 = time.monotonic()
         if self.proc is None:
             return
         self.stop.set()
         try:
             if self.conn.poll(10):
-                self.rows, self.max_mhz = self.conn.recv()
+                rows, self.max_mhz = self.conn.recv()
+                self.rows = [(m, r) for t, m, r in rows if self.t0 <= t <= self.t1]
         except Exception:
             pass
         self.proc.join(timeout=5)
@@ -226,10 +226,10 @@ class Clocks:
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
         mhz = [r[0] for r in self.rows]
-        reasons = sorted({n for _, m, _ in self.rows for n, bit in self.REASONS.items() if m & bit})
+        reasons = sorted({n for _, m in self.rows for n, bit in self.REASONS.items() if m & bit})
         return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(self.rows), "ms_per_sample": 1e3 * statistics.median(r[2] for r in self.rows),
-                "source": "nvml, polled by a child process during the timed steps"}
+                "samples": len(self.rows), "window_ms": round(1e3 * (self.t1 - self.t0), 2),
+                "source": "nvml, polled every ~0.2 ms by a child process during the timed steps"}
 
 
 def peaks():
