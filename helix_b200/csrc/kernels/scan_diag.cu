@@ -256,7 +256,9 @@ __global__ void __launch_bounds__(kDThreads, NS * R <= 32 ? 2 : 1) diag_kernel(S
             __syncthreads();
         }
 
-        // ---- the recurrence over the tile's tokens
+        // ---- the recurrence over the tile's tokens (two per iteration: one
+        // token's y shuffles overlap the next token's loads and arithmetic)
+#pragma unroll 2
         for (int t = 0; t < tlen; ++t) {
             float v[R];
             {
