@@ -362,10 +362,11 @@ def pass_figures(shape, info, ms, hbm, tc):
     b_bytes = runs * st + max(info.n_spans - 1, 0) * st + st + runs * S * H * 4
     # output pass: x, B, C, dt read once, y written once, s0 (or span states) read, s1 written
     c_bytes = S * L * H * P * e + 2 * S * L * G * N * e + S * L * H * 4 + S * L * H * P * 4 + 2 * st
-    # cast pass: x, B, C read as f32, written as bf16 (hi, and lo for the
-    # fp32-class family)
+    # cast pass: B, C (and x, for the bf16 family) read as f32, written as
+    # bf16 (hi, and lo for the fp32-class family, which reads the bench's
+    # dense fp32 x in place)
     planes = 2 if info.family == 2 else 1
-    x_bytes = S * L * (H * P + 2 * G * N)
+    x_bytes = S * L * ((H * P if info.family == 1 else 0) + 2 * G * N)
     x_bytes = x_bytes * 4 + x_bytes * 2 * planes
     out = {}
     for name, by, fl in (("state", a_bytes, a_flops), ("carry", b_bytes, 0.0), ("output", c_bytes, None),
