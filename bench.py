@@ -180,6 +180,7 @@ class Clocks:
     def __init__(self, index: int):
         self.index, self.rows, self.max_mhz, self.proc = index, [], None, None
         self.t0 = self.t1 = None
+        self.polled, self.span_ms = 0, None  # all samples the child took; its first/last vs the window
         try:
             import multiprocessing as mp
             import torch
@@ -217,6 +218,9 @@ class Clocks:
             if self.conn.poll(10):
                 rows, self.max_mhz = self.conn.recv()
                 self.rows = [(m, r) for t, m, r in rows if self.t0 <= t <= self.t1]
+                self.polled = len(rows)
+                if rows:
+                    self.span_ms = (round(1e3 * (rows[0][0] - self.t0), 2), round(1e3 * (rows[-1][0] - self.t1), 2))
         except Exception:
             pass
         self.proc.join(timeout=5)
@@ -224,7 +228,9 @@ class Clocks:
 
     def summary(self):
         if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0,
+                    "polled": self.polled, "first_last_vs_window_ms": self.span_ms,
+                    "window_ms": None if self.t1 is None else round(1e3 * (self.t1 - self.t0), 2)}
         mhz = [r[0] for r in self.rows]
         reasons = sorted({n for _, m in self.rows for n, bit in self.REASONS.items() if m & bit})
         return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
