@@ -4,7 +4,7 @@
 // With a decay that differs per state the masked C.B^T reassociation of the
 // scalar-A families does not exist (reference src/runtime/caps.mm:121-123),
 // so these kernels run the recurrence itself, the fp64 oracle's arithmetic
-// in fp32 (reference src/reference/scan_ref.cpp:27-29, :55-66):
+// in fp32 (reference src/reference/scan_ref.cpp:27-29, :61-65):
 //     s[c][n] = exp(dt_t A[h][n]) s[c][n] + dt_t B_t[n] x_t[c]
 //     y_t[c]  = sum_n C_t[n] s[c][n]
 // in parallel over (sequence, run, group, 64-row tile, state group) and
