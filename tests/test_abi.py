@@ -122,3 +122,30 @@ def test_fp32_tensor_core_scratch_plan_c2():
     d.s_x[0] = 64 * 2 * 64
     d.seq_x = 2048 * 64 * 2 * 64
     assert lib.helix_scan_scratch_size(None, C.byref(d)) == agg + lam + al(2048 * 64 * 64 * 4) + 4 * bc
+
+
+def test_diagonal_a_scratch_plan():
+    """Diagonal A (one rate per (head, state)) on a 148-SM part: one output
+    CTA per 64 (head, channel) rows of a group, runs cut so the output kernel
+    has about four CTAs per SM; scratch = one run state and one dt sum per run
+    before the last, no copies.  Config 3's shape: 64 tiles -> 10 runs of 896
+    tokens; a Mamba-1 layer (2048 heads of head_dim 1, d_state 16, one group):
+    32 tiles -> 16 runs of 512 tokens; single pass needs none."""
+    lib = abi.load()
+
+    def al(n):
+        return (n + 255) // 256 * 256
+
+    def desc(L, S, H, P, N, G, multipass=True):
+        d = abi.desc_init(L, S, H, P, N, G)
+        d.a_form = abi.HELIX_A_DIAG_PER_CHANNEL
+        d.s_a = N
+        d.multipass = multipass
+        return d
+
+    d = desc(8192, 1, 64, 64, 128, 8)
+    assert lib.helix_scan_scratch_size(None, C.byref(d)) == al(64 * 9 * 64 * 128 * 4) + al(64 * 9 * 4)
+    d = desc(8192, 1, 2048, 1, 16, 1)
+    assert lib.helix_scan_scratch_size(None, C.byref(d)) == al(2048 * 15 * 1 * 16 * 4) + al(2048 * 15 * 4)
+    d = desc(8192, 1, 64, 64, 128, 8, multipass=False)
+    assert lib.helix_scan_scratch_size(None, C.byref(d)) == 0

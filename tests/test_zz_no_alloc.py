@@ -12,6 +12,7 @@ oracle on the same inputs, within the bounds the parity suites use:
     with one chunk of extreme decay routing tiles of the tensor-core family
     through the general path (which reads the run spans and tile flags from
     the shared array);
+  * diagonal A (the recurrence kernels' run states and dt sums in the array);
   * in a fresh process, the array is reserved by the first call and not
     before (lazy module loading).
 This file sorts last so that a run that stops at the first failure has
@@ -141,6 +142,29 @@ def test_static_general_path_forced(ctx, oracle, env):
     env("HELIX_TC_GENERAL", "1")
     shape = (1536, 1, 4, 64, 128, 2)
     _check_call(ctx, oracle, _problem(oracle, 31, *shape), shape, "bf16", "bf16 forced general")
+
+
+def test_static_diagonal_a(ctx, oracle, env):
+    """Diagonal A through the static array: its run states and dt sums."""
+    from oracle.oracle import diag_desc
+    env("HELIX_RUN_TOKENS", "256")
+    shape = (1000, 2, 8, 64, 64, 2)
+    L, S, H, P, N, G = shape
+    dev = torch.device("cuda:0")
+    prob = oracle.harness_problem_diag(*shape, 41, True)
+    t = _torch(prob, torch.float32, dev)
+    d = helix_b200.desc_from_tensors(t["x"], t["dt"], t["B"], t["s0"], multipass=True, A=t["A"])
+    assert d.a_form == abi.HELIX_A_DIAG_PER_CHANNEL and 0 < ctx.scratch_size(d) <= (32 << 20)
+    for call in range(2):
+        y = torch.full((S, L, H, P), float("nan"), device=dev)
+        s1 = torch.full((S, H, P, N), float("nan"), device=dev)
+        assert _static(ctx, d, t, y, s1) == abi.HELIX_OK, ctx.last_error()
+        torch.cuda.synchronize()
+        y_ref, s_ref = oracle.scan(diag_desc(oracle.desc_init(*shape)),
+                                   *[prob[k] for k in ("s0", "x", "dt", "A", "B", "C")])
+        for name, got, want in (("y", y, y_ref), ("s1", s1, s_ref)):
+            c = compare(got.cpu().numpy(), want, X3_REL, X3_ABS)
+            assert c["ok"] and c["rel_l2"] <= X3_RL2, ("diag", call, name, c)
 
 
 def test_static_scratch_rejects_oversized(ctx, cuda, env):
