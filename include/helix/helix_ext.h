@@ -101,7 +101,10 @@ helix_status helix_scan_plan_info(helix_ctx* ctx, const helix_scan_desc* d, heli
  * helix_scan_shard_state computes in d's precision path (compute_dtype,
  * backend) and needs helix_scan_shard_state_scratch_size() bytes of
  * 256-byte-aligned scratch (multipass is implied).  Both are enqueued on
- * `stream` and never synchronise or allocate. */
+ * `stream` and never synchronise or allocate.  The token-shard entry points
+ * need scalar A (a_form HELIX_A_SCALAR_PER_HEAD): with a rate per state a
+ * shard's decay is not one scalar per (seq, head), and they return
+ * HELIX_ERR_UNSUPPORTED_SHAPE. */
 size_t helix_scan_shard_state_scratch_size(helix_ctx* ctx, const helix_scan_desc* d);
 
 helix_status helix_scan_shard_state(helix_ctx*             ctx,
