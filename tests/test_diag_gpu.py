@@ -163,6 +163,35 @@ def test_strided_x_and_y_diag(ctx, oracle):
     _check("diag strided x, y", y.cpu().numpy(), s1.cpu().numpy(), y_ref, s_ref)
 
 
+def test_padded_a_rows(ctx, oracle):
+    """A read through a view whose head rows are d_state + 3 floats apart
+    (s_a = d_state + 3): the kernels index A[h * s_a + n]."""
+    import torch
+    import helix_b200
+    shape = (300, 1, 4, 32, 64, 2)  # head_dim 32: tiles span two heads (per-lane rates)
+    L, S, H, P, N, G = shape
+    prob = oracle.harness_problem_diag(*shape, 5, True)
+    y_ref, s_ref = _oracle(oracle, prob, shape)
+    dev = torch.device("cuda:0")
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in prob.items()}
+    big = torch.full((H, N + 3), float("nan"), device=dev)
+    A = big[:, :N]
+    A.copy_(t["A"])
+    y, s1 = helix_b200.scan(t["x"], t["dt"], A, t["B"], t["C"], t["s0"], ctx=ctx)
+    torch.cuda.synchronize()
+    _check("diag padded A rows", y.cpu().numpy(), s1.cpu().numpy(), y_ref, s_ref)
+    for uni_shape in ((300, 1, 2, 64, 64, 1),):  # head_dim 64: one head per tile (staged decays)
+        prob = oracle.harness_problem_diag(*uni_shape, 6, True)
+        y_ref, s_ref = _oracle(oracle, prob, uni_shape)
+        t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in prob.items()}
+        big = torch.full((uni_shape[2], uni_shape[4] + 3), float("nan"), device=dev)
+        A = big[:, :uni_shape[4]]
+        A.copy_(t["A"])
+        y, s1 = helix_b200.scan(t["x"], t["dt"], A, t["B"], t["C"], t["s0"], ctx=ctx)
+        torch.cuda.synchronize()
+        _check("diag padded A rows, one head per tile", y.cpu().numpy(), s1.cpu().numpy(), y_ref, s_ref)
+
+
 def test_high_level_scan_reads_the_a_form(oracle):
     """helix_b200.scan takes A of shape (n_head, d_state) as diagonal A."""
     import torch
